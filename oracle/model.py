@@ -1,0 +1,170 @@
+"""Oracle: VGGT aggregator block math (CPU, PyTorch fp32 with fp16 rounding points).
+
+TEST INFRASTRUCTURE ONLY -- see ``oracle/__init__.py``.
+
+The aggregator itself lives in the un-vendored ``vggt-hf`` fork that the
+reference imports (``qvggt/inference/loader.py:27``); its semantics are restated
+here from the published VGGT algorithm and BASELINE config 1:
+
+    x = x + ls1 * proj(attn(rope2d(q), rope2d(k), v)),  q,k,v = qkv(LN1(x))
+    x = x + ls2 * fc2(gelu(fc1(LN2(x))))
+
+pre-LayerNorm eps 1e-6, 16 heads x 64, LayerScale gamma, exact-erf GELU, 2-D
+RoPE base 100, optional per-head q/k LayerNorm (``qk_norm``, off by default).
+Every tensor that eager fp16 PyTorch would materialise is rounded to fp16 at
+the same point; matmuls and reductions run in fp32.
+
+The quantised linears follow ``WQLinear.forward`` (``qmodule.py:333-369``):
+fp16 GEMM output, then a separate fp16 bias add.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from . import awq, rope
+
+F16 = torch.float16
+
+
+def r16(x: torch.Tensor) -> torch.Tensor:
+    return x.to(F16)
+
+
+def layernorm(x: torch.Tensor, w, b, eps: float = 1e-6) -> torch.Tensor:
+    """fp16 in -> fp32 math -> fp16 out (as ``nn.LayerNorm`` on fp16)."""
+    xf = x.float()
+    mu = xf.mean(-1, keepdim=True)
+    var = ((xf - mu) ** 2).mean(-1, keepdim=True)
+    y = (xf - mu) * torch.rsqrt(var + eps)
+    y = y * torch.as_tensor(w).float() + torch.as_tensor(b).float()
+    return r16(y)
+
+
+def gelu_erf(x: torch.Tensor) -> torch.Tensor:
+    xf = x.float()
+    return r16(0.5 * xf * (1.0 + torch.erf(xf / math.sqrt(2.0))))
+
+
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, chunk: int = 4096) -> torch.Tensor:
+    """softmax(q k^T / sqrt(d)) v in fp32, q/k/v [..., L, d] fp16 -> fp16."""
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d)
+    kf, vf = k.float(), v.float()
+    outs = []
+    for s in range(0, q.shape[-2], chunk):
+        qf = q[..., s:s + chunk, :].float()
+        a = torch.softmax((qf @ kf.transpose(-1, -2)) * scale, dim=-1)
+        outs.append(a @ vf)
+    return r16(torch.cat(outs, dim=-2))
+
+
+class QLinear:
+    """One linear in the W4A16 (``kind='w4'``), dense fp16 (``'f16'``) or
+    W8A8 (``'w8'``) form, holding exactly the buffers the GPU path uses."""
+
+    def __init__(self, kind: str, **bufs):
+        self.kind = kind
+        self.__dict__.update(bufs)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """fp16 [.., K] -> fp16 [.., N] including the bias."""
+        if self.kind == "w4":
+            return awq.wqlinear_forward_fp16(x, self.qweight, self.scales, self.scaled_zeros,
+                                             self.group_size, self.bias)
+        if self.kind == "f16":
+            y = r16(x.reshape(-1, x.shape[-1]).float() @ torch.as_tensor(self.weight).float().t())
+            if self.bias is not None:
+                y = r16(y.float() + torch.as_tensor(self.bias).float())
+            return y.reshape(*x.shape[:-1], -1)
+        raise ValueError(self.kind)
+
+
+def random_w4_linear(K: int, N: int, gen: np.random.Generator, group_size: int = 128,
+                     w_std: float = 0.02) -> QLinear:
+    """Random-init nn.Linear weights N(0, w_std), quantised W4A16 the AWQ way
+    (asymmetric per group: s = (max-min)/15, z = round(-min/s))."""
+    G = group_size
+    w = gen.standard_normal((N, K)).astype(np.float32) * w_std
+    wg = w.reshape(N, K // G, G)
+    mx, mn = wg.max(-1), wg.min(-1)
+    s = np.maximum((mx - mn) / 15.0, 1e-5).astype(np.float16)
+    z = np.clip(np.round(-mn / s.astype(np.float32)), 0, 15).astype(np.float32)
+    q = np.clip(np.round(wg / s.astype(np.float32)[..., None] + z[..., None]), 0, 15).astype(np.int32)
+    q = q.reshape(N, K)
+    gpad = awq.calculate_zeros_width(K, G) * 8
+    st = np.zeros((gpad, N), np.float16)
+    st[: K // G] = s.T
+    szt = np.zeros((gpad, N), np.float16)
+    szt[: K // G] = (-(s.astype(np.float32) * z)).astype(np.float16).T
+    bias = (gen.standard_normal(N) * 0.01).astype(np.float16)
+    return QLinear("w4", qweight=awq.pack_intweight(q), scales=st, scaled_zeros=szt, bias=bias,
+                   group_size=G, in_features=K, out_features=N)
+
+
+def random_f16_linear(K: int, N: int, gen: np.random.Generator, w_std: float = 0.02) -> QLinear:
+    w = (gen.standard_normal((N, K)) * w_std).astype(np.float16)
+    bias = (gen.standard_normal(N) * 0.01).astype(np.float16)
+    return QLinear("f16", weight=w, bias=bias, in_features=K, out_features=N)
+
+
+def random_block(gen: np.random.Generator, dim: int = 1024, mlp: int = 4096, kind: str = "w4",
+                 ls: float = 0.01, qk_norm: bool = False, head_dim: int = 64) -> dict:
+    mk = (lambda K, N: random_w4_linear(K, N, gen)) if kind == "w4" else (lambda K, N: random_f16_linear(K, N, gen))
+    blk = dict(
+        norm1_w=(1.0 + 0.1 * gen.standard_normal(dim)).astype(np.float16),
+        norm1_b=(0.1 * gen.standard_normal(dim)).astype(np.float16),
+        qkv=mk(dim, 3 * dim), proj=mk(dim, dim),
+        ls1=np.full(dim, ls, np.float16),
+        norm2_w=(1.0 + 0.1 * gen.standard_normal(dim)).astype(np.float16),
+        norm2_b=(0.1 * gen.standard_normal(dim)).astype(np.float16),
+        fc1=mk(dim, mlp), fc2=mk(mlp, dim),
+        ls2=np.full(dim, ls, np.float16),
+        qk_norm=qk_norm,
+    )
+    if qk_norm:
+        blk.update(qn_w=(1.0 + 0.1 * gen.standard_normal(head_dim)).astype(np.float16),
+                   qn_b=(0.1 * gen.standard_normal(head_dim)).astype(np.float16),
+                   kn_w=(1.0 + 0.1 * gen.standard_normal(head_dim)).astype(np.float16),
+                   kn_b=(0.1 * gen.standard_normal(head_dim)).astype(np.float16))
+    return blk
+
+
+def block_forward(x: torch.Tensor, blk: dict, pos: torch.Tensor | None, heads: int = 16,
+                  eps: float = 1e-6, attn_fn=None) -> torch.Tensor:
+    """One pre-LN transformer block over x [B, L, C] fp16 with positions pos [L, 2]
+    (``None`` disables RoPE).  Returns fp16 [B, L, C]."""
+    B, L, C = x.shape
+    hd = C // heads
+    h = layernorm(x, blk["norm1_w"], blk["norm1_b"], eps)
+    qkv = blk["qkv"](h).reshape(B, L, 3, heads, hd).permute(2, 0, 3, 1, 4)
+    q, k, v = qkv[0], qkv[1], qkv[2]
+    if blk.get("qk_norm"):
+        q = layernorm(q, blk["qn_w"], blk["qn_b"], eps)
+        k = layernorm(k, blk["kn_w"], blk["kn_b"], eps)
+    if pos is not None:
+        q = rope.rope2d(q, pos)
+        k = rope.rope2d(k, pos)
+    o = (attn_fn or sdpa)(q, k, v)
+    o = o.transpose(1, 2).reshape(B, L, C)
+    y = blk["proj"](o)
+    x = r16(x.float() + r16(y.float() * torch.as_tensor(blk["ls1"]).float()).float())
+    h2 = layernorm(x, blk["norm2_w"], blk["norm2_b"], eps)
+    f = gelu_erf(blk["fc1"](h2))
+    y2 = blk["fc2"](f)
+    return r16(x.float() + r16(y2.float() * torch.as_tensor(blk["ls2"]).float()).float())
+
+
+def block_pair_forward(tokens: torch.Tensor, frame_blk: dict, global_blk: dict,
+                       patch_start: int = 5, grid_w: int = 37) -> tuple[torch.Tensor, torch.Tensor]:
+    """Frame block over [S, P, C] then global block over [1, S*P, C].
+
+    Returns (frame_out [S, P, C], global_out [S, P, C]).
+    """
+    S, P, C = tokens.shape
+    pos = rope.patch_positions(P, patch_start, grid_w)
+    xf = block_forward(tokens, frame_blk, pos)
+    xg = block_forward(xf.reshape(1, S * P, C), global_blk, pos.repeat(S, 1))
+    return xf, xg.reshape(S, P, C)
