@@ -1,0 +1,185 @@
+/*
+ * qvggt_b200 -- C ABI of the B200 (sm_100a) kernels for QVGGT's quantised
+ * transformer hot path.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream) and returns
+ * QVGGT_OK or an error code; qvggt_last_error() gives the message of the last
+ * failure on the calling thread.  Kernels are launched asynchronously on the
+ * stream; nothing here synchronises.  Tensors are dense row-major unless a
+ * stride argument says otherwise.  fp16 means IEEE binary16.
+ *
+ * Reference citations are paths inside the QVGGT repository
+ * (E/ = qvggt/runtime/awq_inference_engine/csrc/).
+ */
+#ifndef QVGGT_B200_H
+#define QVGGT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QVGGT_OK 0
+#define QVGGT_ERR_INVALID 1      /* bad shape or argument */
+#define QVGGT_ERR_UNSUPPORTED 2  /* configuration the kernels do not implement */
+#define QVGGT_ERR_CUDA 3         /* CUDA runtime / launch error */
+#define QVGGT_ERR_TIMEOUT 4      /* a bounded device-side wait gave up */
+#define QVGGT_ERR_ALIGN 5        /* pointer or stride not 16-byte aligned */
+
+#define QVGGT_DTYPE_F16 0
+
+/* Library version (major*10000 + minor*100 + patch). */
+int qvggt_version(void);
+
+/* Message of the last error returned on this thread ("" if none). */
+const char* qvggt_last_error(void);
+
+/* Device status word of the current device: 0, or the code of the first
+ * bounded device-side wait that gave up since the last clear.  Synchronises
+ * the current device.  clear != 0 resets the word to 0 afterwards. */
+int qvggt_device_status(uint32_t* status_out, int clear);
+
+/* Budget of every bounded device-side wait (default 2 s). */
+int qvggt_set_wait_timeout_ns(uint64_t ns);
+
+/* Number of kernels this library launched on this process (all devices). */
+uint64_t qvggt_launch_count(void);
+
+/* ---------------------------------------------------------------- W4A16 */
+
+/* out[M, N] = in_feats[M, K] . deq(qweight)^T (+ bias), fp16 in / fp16 out,
+ * fp32 accumulation (tcgen05, TMEM).  qweight int16 [N/4, K] in the AWQ
+ * interleaved layout of pack_intweight(interleave=4, kstride=64);
+ * scales / scaled_zeros fp16 [gpad, N], gpad >= K / group_size.
+ * Requirements: N % 128 == 0, K % group_size == 0, group_size % 64 == 0.
+ * bias may be NULL; with a bias the result is half(half(acc) + bias), the same
+ * two roundings as the reference's GEMM followed by `out + self.bias`.
+ * Replaces gemm_forward_cuda_new (E/quantization_new/gemm/gemm_cuda.cu:1125-1235,
+ * bound at E/pybind.cpp:21) and the bias add of WQLinear.forward
+ * (qvggt/runtime/awq/qmodule.py:361-367). */
+int qvggt_w4a16_gemm(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                     const void* bias, void* out, int64_t M, int64_t N, int64_t K, int64_t gpad,
+                     int32_t group_size, void* stream);
+
+/* Same GEMM with a fused epilogue for the VGGT block:
+ *   act == 1: out = gelu_erf(half(half(acc) + bias))          (fc1 -> GELU)
+ *   resid != NULL: resid[M, ldr] += half(half(half(acc)+bias) * gamma)
+ *                  (out must equal resid; LayerScale residual of proj / fc2)
+ * New entry point (the reference runs these as separate PyTorch ops after
+ * WQLinear.forward, qmodule.py:333-369). */
+int qvggt_w4a16_linear_ex(const void* in_feats, int64_t lda, const void* qweight, const void* scales,
+                          const void* scaled_zeros, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
+                          int64_t K, int64_t gpad, int32_t group_size, int32_t act, const void* resid,
+                          int64_t ldr, const void* gamma, void* stream);
+
+/* Dense fp16 linear with the same fused epilogues (weight fp16 [N, K]); used
+ * for the unquantised DINOv2 patch-embed blocks.  No reference counterpart
+ * (the reference runs these layers in PyTorch). */
+int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, const void* bias, void* out,
+                        int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
+                        const void* gamma, void* stream);
+
+/* out[m, N] = in_feats[m, K] . deq(qweight)^T (+ bias) for 1 <= m <= 16.
+ * Any group_size that is a multiple of 32 and divides K.
+ * Replaces gemv_forward_cuda_new (E/quantization_new/gemv/gemv_cuda.cu:197-281,
+ * bound at E/pybind.cpp:22; reference: m <= 7, group_size 128 only). */
+int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                     const void* bias, void* out, int64_t m, int64_t N, int64_t K, int64_t gpad,
+                     int32_t group_size, void* stream);
+
+/* ----------------------------------------------------------------- W8A8 */
+
+/* out[M, N] fp16 = half(float(acc) * (wscales[n] * ascales[m]))                (bias == NULL)
+ *              or half(fma(float(acc) * wscales[n], ascales[m], bias[n]))      (bias != NULL)
+ * acc = sum_k in[m, k] * w[n, k] in int32 (tcgen05 kind::i8, TMEM).
+ * in int8 [M, K], w int8 [N, K], wscales fp16 [N], ascales fp16 [M].
+ * Requirements: N % 128 == 0, K % 128 == 0.
+ * Replaces w8a8_gemm_forward_cuda and w8a8_gemm_fuse_bias_forward_cuda
+ * (E/w8a8/w8a8_gemm_cuda.cu:881-922 and :564-607, E/pybind.cpp:27-28). */
+int qvggt_w8a8_gemm(const int8_t* in, const int8_t* w, const void* wscales, const void* ascales, const void* bias,
+                    void* out, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Raw int32 accumulators acc[M, N] of the same GEMM (for bit-exact checks).
+ * No reference counterpart (the reference never exposes its accumulators). */
+int qvggt_i8_gemm_i32(const int8_t* in, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                      void* stream);
+
+/* Per-token dynamic int8 quantisation: scale[t] = half(amax_t / 127),
+ * out = rni_sat(x * (127 / amax_t)).  in fp16 [tokens, hidden].
+ * Replaces invoke_quant (E/w8a8/quantization.cu:81-96, E/pybind.cpp:29). */
+int qvggt_invoke_quant(int8_t* out, const void* in, void* scale, int64_t tokens, int64_t hidden, void* stream);
+
+/* LayerNorm (var = E[x^2] - E[x]^2) + int8 quantisation.
+ * per_token != 0: out = rni_sat(ln * 127 / amax), scale_io[t] = half(amax/127)
+ *   (amax over fp16-rounded ln, floor half(1e-6)); beta used.
+ * per_token == 0: out = rni_sat(half(ln) * scale_io[0]) with scale_io a
+ *   per-tensor fp16 input; beta ignored (the reference passes none).
+ * Replaces rms_norm_general (E/w8a8/layernorm.cu:155-191, E/pybind.cpp:30-32). */
+int qvggt_layernorm_quant(int8_t* out, const void* in, const void* gamma, const void* beta, void* scale_io,
+                          int64_t tokens, int64_t hidden, float eps, int32_t per_token, void* stream);
+
+/* tmp = gelu_tanh(in) in fp16 arithmetic; scale[t] = half(amax_t / 127) with
+ * the reference's |t| rule (t > 1e-4 ? t : -t); out = rni_sat(half(127/amax) * tmp).
+ * Replaces gelu_and_quant (E/w8a8/act.cu:77-90, E/pybind.cpp:36). */
+int qvggt_gelu_quant(int8_t* out, const void* in, void* scale, void* tmp, int64_t tokens, int64_t d, void* stream);
+
+/* ---------------------------------------------------------------- norms */
+
+/* out = LayerNorm(in) * gamma + beta, fp16 in/out, fp32 statistics
+ * (two-pass mean / variance).  rows of `hidden` (multiple of 256, <= 8192).
+ * New entry point: the VGGT pre-norm (nn.LayerNorm, run by PyTorch in the
+ * reference model). */
+int qvggt_layernorm(const void* in, const void* gamma, const void* beta, void* out, int64_t tokens, int64_t hidden,
+                    float eps, void* stream);
+
+/* ----------------------------------------------------------------- RoPE */
+
+/* Reference rotate-half RoPE with explicit per-(b, s) angles:
+ * in [s, b, h, d] with element strides in_strides[4], freqs fp32 [b, s, d2],
+ * out [s, b, h, d] with element strides out_strides[4]; dims >= d2 copied.
+ * Replaces fused_rope_with_pos_forward_func (E/rope_new/fused_rope_with_pos.cu:122-164,
+ * E/pybind.cpp:26); the caller allocates `out` with the strides it wants. */
+int qvggt_rope_with_pos(const void* in, const float* freqs, void* out, int64_t s, int64_t b, int64_t h, int64_t d,
+                        int64_t d2, const int64_t* in_strides, const int64_t* out_strides, void* stream);
+
+/* VGGT 2-D RoPE fused with the q/k/v split of the qkv projection output.
+ * qkv fp16 [T, 3*H*64] (token-major, [q | k | v], head-major inside each);
+ * q_out [T, H*64] (roped), kv_out [T, 2*H*64] ([k roped | v]).
+ * Token t's position: p = (t + token_offset) % tokens_per_frame; p < patch_start
+ * -> (0, 0) else ((p-patch_start)/grid_w + 1, (p-patch_start)%grid_w + 1).
+ * cos_tab / sin_tab fp16 [max_pos, 32] (the per-half tables of the model).
+ * qk_norm != 0 applies LayerNorm over each head's 64 dims to q and k first
+ * (weights qn_w/qn_b/kn_w/kn_b fp16 [64]).  New entry point. */
+int qvggt_qkv_rope2d(const void* qkv, void* q_out, void* kv_out, int64_t T, int32_t heads, int64_t token_offset,
+                     int32_t tokens_per_frame, int32_t patch_start, int32_t grid_w, const void* cos_tab,
+                     const void* sin_tab, int32_t max_pos, int32_t qk_norm, const void* qn_w, const void* qn_b,
+                     const void* kn_w, const void* kn_b, float eps, void* stream);
+
+/* ------------------------------------------------------------ attention */
+
+/* Flash attention, head_dim 64, non-causal, softmax(q k^T / 8) v, tcgen05.
+ * Token-major layouts: q [batches*Lq rows, q_stride] with head h at column
+ * h*64; k / v rows of kv_stride elements, head h at k_col0 + h*64 and
+ * v_col0 + h*64; out [batches*Lq, o_stride], head h at column h*64.
+ * Batch b covers q rows [b*Lq, (b+1)*Lq) and kv rows [b*Lkv, (b+1)*Lkv).
+ * Strides are in elements and must be multiples of 8.
+ * New entry point (the reference model runs PyTorch SDPA). */
+int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                    int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
+                    int32_t heads, void* stream);
+
+/* ------------------------------------------------------------- self-test */
+
+/* Runs one kernel whose bounded wait waits on an mbarrier nothing arrives on;
+ * it must give up after the wait budget and report QVGGT_ERR_TIMEOUT through
+ * the status word (which this call clears).  Synchronises.  For tests of the
+ * failure path; faults nothing. */
+int qvggt_selftest_wait_timeout(uint64_t timeout_ns, uint32_t* status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QVGGT_B200_H */

@@ -86,13 +86,17 @@ def rms_norm_general(x, gamma, beta, eps: float):
 
 
 def gelu_fast_h(x):
-    """fp16 tanh-GELU ``gelu_fast<half>`` (``w8a8/act.cu:22-28``), op by op in fp16."""
+    """fp16 tanh-GELU ``gelu_fast<half>`` (``w8a8/act.cu:22-28``), op by op in fp16.
+
+    ``(T)1.0 + (T)(0.044715 * f) * x`` is a half multiply followed by a half
+    add, which nvcc contracts (default -fmad=true) into one fp16 fma: one
+    rounding of b*x + 1.
+    """
     x = np.asarray(x, dtype=F16)
     f = x
     a = hmul(F16(0.79788456), f)
     b = hmul(F16(0.044715), f)
-    c = hmul(b, x)
-    d = hadd(F16(1.0), c)
+    d = h(b.astype(np.float64) * x.astype(np.float64) + 1.0)
     e = hmul(a, d)
     t = h(np.tanh(e.astype(np.float64)))
     half_x = hmul(F16(0.5), x)

@@ -1,0 +1,332 @@
+"""Drop-in replacement of the reference's ``awq_inference_engine`` extension.
+
+Same function names, argument order, dtypes, layouts and ownership as the
+bindings in ``qvggt/runtime/awq_inference_engine/csrc/pybind.cpp:18-36``; every
+op runs a sm_100a kernel of ``libqvggt_b200.so`` through its C ABI on the
+current PyTorch CUDA stream of the tensor's device.  There is no CPU path:
+CPU tensors, wrong dtypes or unsupported shapes raise.
+
+Ops outside the VGGT hot path (``layernorm_forward_cuda`` = T5 RMSNorm,
+``rotary_embedding_neox`` = 1-D LLM RoPE, ``single_query_attention`` =
+decode-time attention, ``silu_and_mul`` = SwiGLU) raise ``NotImplementedError``.
+
+New ops of the hot path (no reference name): :func:`w4a16_linear`,
+:func:`f16_linear`, :func:`layernorm`, :func:`qkv_rope2d`, :func:`attention`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "gemm_forward_cuda_new", "gemv_forward_cuda_new", "w8a8_gemm_forward_cuda",
+    "w8a8_gemm_fuse_bias_forward_cuda", "invoke_quant", "rms_norm_general", "gelu_and_quant",
+    "fused_rope_with_pos_forward_func", "w4a16_linear", "f16_linear", "layernorm", "qkv_rope2d",
+    "attention", "i8_gemm_i32",
+]
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor):
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _check_cuda(name, *ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{name}: all tensors must be CUDA tensors (no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{name}: tensors on different devices")
+    return dev
+
+
+def _check_dtype(name, t, *dtypes):
+    if t is not None and t.dtype not in dtypes:
+        raise TypeError(f"{name}: expected {dtypes}, got {t.dtype}")
+
+
+def _contig(name, *ts):
+    for t in ts:
+        if t is not None and not t.is_contiguous():
+            raise ValueError(f"{name}: tensors must be contiguous")
+
+
+class _Dev:
+    def __init__(self, dev):
+        self.g = torch.cuda.device(dev)
+
+    def __enter__(self):
+        self.g.__enter__()
+
+    def __exit__(self, *a):
+        self.g.__exit__(*a)
+
+
+# --------------------------------------------------------------------- W4A16
+def gemm_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, group_size: int = 128):
+    """C = in_feats . deq(qweight)^T (``gemm_cuda.cu:1125-1235``).
+
+    in_feats fp16 [..., K]; qweight int16 [N/4, K]; scales / scaled_zeros fp16
+    [gpad, N].  Returns a new fp16 tensor [..., N].  The reference fixes the
+    group size at 128; it is a keyword here for other multiples of 64.
+    """
+    name = "gemm_forward_cuda_new"
+    dev = _check_cuda(name, in_feats, qweight, scales, scaled_zeros)
+    _check_dtype(name, in_feats, torch.float16)
+    _check_dtype(name, scales, torch.float16)
+    _check_dtype(name, scaled_zeros, torch.float16)
+    _check_dtype(name, qweight, torch.int16)
+    _contig(name, in_feats, qweight, scales, scaled_zeros)
+    K = in_feats.shape[-1]
+    N = qweight.shape[0] * 4
+    if qweight.shape[1] != K:
+        raise ValueError(f"{name}: qweight {tuple(qweight.shape)} does not match K={K}")
+    M = in_feats.numel() // K
+    out = torch.empty(*in_feats.shape[:-1], N, dtype=in_feats.dtype, device=dev)
+    with _Dev(dev):
+        _lib.call("qvggt_w4a16_gemm", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
+                  _ptr(out), M, N, K, scales.shape[0], group_size, _stream(in_feats))
+    return out
+
+
+def gemv_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, m: int, n: int, k: int, group_size: int):
+    """y = in_feats . deq(qweight)^T for m <= 16 rows (``gemv_cuda.cu:197-281``)."""
+    name = "gemv_forward_cuda_new"
+    dev = _check_cuda(name, in_feats, qweight, scales, scaled_zeros)
+    _check_dtype(name, in_feats, torch.float16)
+    _check_dtype(name, scales, torch.float16)
+    _check_dtype(name, scaled_zeros, torch.float16)
+    _contig(name, in_feats, qweight, scales, scaled_zeros)
+    if not (1 <= m <= 16):
+        raise RuntimeError("Unsupported batch size for gemv kernel.")
+    if group_size % 32 or k % group_size:
+        raise RuntimeError("Unsupported group size for gemv kernel.")
+    out = torch.empty(*in_feats.shape[:-1], n, dtype=in_feats.dtype, device=dev)
+    with _Dev(dev):
+        _lib.call("qvggt_w4a16_gemv", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
+                  _ptr(out), m, n, k, scales.shape[0], group_size, _stream(in_feats))
+    return out
+
+
+def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 128, act: str | None = None,
+                 residual=None, gamma=None, out=None):
+    """Fused W4A16 linear: ``half(half(x.W^T) + bias)`` then optionally
+    ``gelu`` (act='gelu') or an in-place LayerScale residual update
+    ``residual += half(y * gamma)`` (returns ``residual``).  m <= 16 rows use
+    the GEMV kernel (plain / bias epilogue only)."""
+    name = "w4a16_linear"
+    dev = _check_cuda(name, x, qweight, scales, scaled_zeros, bias, residual, gamma)
+    _contig(name, x, qweight, scales, scaled_zeros, bias, gamma)
+    K = x.shape[-1]
+    N = qweight.shape[0] * 4
+    M = x.numel() // K
+    if residual is not None:
+        out = residual
+    elif out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
+    with _Dev(dev):
+        if M <= 16 and act is None and residual is None:
+            _lib.call("qvggt_w4a16_gemv", _ptr(x), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), _ptr(bias),
+                      _ptr(out), M, N, K, scales.shape[0], group_size, _stream(x))
+        else:
+            _lib.call("qvggt_w4a16_linear_ex", _ptr(x), K, _ptr(qweight), _ptr(scales), _ptr(scaled_zeros),
+                      _ptr(bias), _ptr(out), N, M, N, K, scales.shape[0], group_size, 1 if act == "gelu" else 0,
+                      _ptr(residual), N if residual is not None else 0, _ptr(gamma), _stream(x))
+    return out
+
+
+def f16_linear(x, weight, bias=None, act: str | None = None, residual=None, gamma=None, out=None):
+    """Dense fp16 linear (weight [N, K]) with the same fused epilogues."""
+    name = "f16_linear"
+    dev = _check_cuda(name, x, weight, bias, residual, gamma)
+    _contig(name, x, weight, bias, gamma)
+    K = x.shape[-1]
+    N = weight.shape[0]
+    M = x.numel() // K
+    if residual is not None:
+        out = residual
+    elif out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
+    with _Dev(dev):
+        _lib.call("qvggt_f16_linear_ex", _ptr(x), K, _ptr(weight), _ptr(bias), _ptr(out), N, M, N, K,
+                  1 if act == "gelu" else 0, _ptr(residual), N if residual is not None else 0, _ptr(gamma),
+                  _stream(x))
+    return out
+
+
+# ---------------------------------------------------------------------- W8A8
+def _w8a8(name, in_feats, kernel, wscales, ascales, out, bias):
+    dev = _check_cuda(name, in_feats, kernel, wscales, ascales, out, bias)
+    _check_dtype(name, in_feats, torch.int8)
+    _check_dtype(name, kernel, torch.int8)
+    _check_dtype(name, out, torch.float16)
+    _contig(name, in_feats, kernel, wscales, ascales, out, bias)
+    M, K = in_feats.shape[0], in_feats.shape[1]
+    N = out.shape[-1]
+    with _Dev(dev):
+        _lib.call("qvggt_w8a8_gemm", _ptr(in_feats), _ptr(kernel), _ptr(wscales), _ptr(ascales), _ptr(bias),
+                  _ptr(out), M, N, K, _stream(in_feats))
+
+
+def w8a8_gemm_forward_cuda(in_feats, kernel, wscales, ascales, out_feats):
+    """out = half(float(acc) * (ws * as)) (``w8a8_gemm_cuda.cu:881-922``); writes out_feats."""
+    _w8a8("w8a8_gemm_forward_cuda", in_feats, kernel, wscales, ascales, out_feats, None)
+
+
+def w8a8_gemm_fuse_bias_forward_cuda(in_feats, kernel, wscales, ascales, out_feats, bias):
+    """out = half(fma(acc * ws, as, bias)) (``w8a8_gemm_cuda.cu:564-607``); writes out_feats."""
+    _w8a8("w8a8_gemm_fuse_bias_forward_cuda", in_feats, kernel, wscales, ascales, out_feats, bias)
+
+
+def i8_gemm_i32(in_feats, kernel):
+    """Raw int32 accumulators of the int8 GEMM (for bit-exact checks)."""
+    name = "i8_gemm_i32"
+    dev = _check_cuda(name, in_feats, kernel)
+    _contig(name, in_feats, kernel)
+    M, K = in_feats.shape
+    N = kernel.shape[0]
+    acc = torch.empty(M, N, dtype=torch.int32, device=dev)
+    with _Dev(dev):
+        _lib.call("qvggt_i8_gemm_i32", _ptr(in_feats), _ptr(kernel), _ptr(acc), M, N, K, _stream(in_feats))
+    return acc
+
+
+def invoke_quant(out, input, scale):
+    """Per-token int8 quantisation (``quantization.cu:81-96``); writes out and scale."""
+    name = "invoke_quant"
+    dev = _check_cuda(name, out, input, scale)
+    _check_dtype(name, input, torch.float16)
+    _contig(name, out, input, scale)
+    H = input.shape[-1]
+    with _Dev(dev):
+        _lib.call("qvggt_invoke_quant", _ptr(out), _ptr(input), _ptr(scale), input.numel() // H, H, _stream(input))
+
+
+def rms_norm_general(out, input, weight, bias, scaling, epsilon: float, use_per_token_quant: bool = True):
+    """LayerNorm + int8 quantisation (``w8a8/layernorm.cu:155-191``); writes out and scaling."""
+    name = "rms_norm_general"
+    dev = _check_cuda(name, out, input, weight, bias, scaling)
+    _check_dtype(name, input, torch.float16)
+    _contig(name, out, input, weight, bias, scaling)
+    H = input.shape[-1]
+    with _Dev(dev):
+        _lib.call("qvggt_layernorm_quant", _ptr(out), _ptr(input), _ptr(weight), _ptr(bias), _ptr(scaling),
+                  input.numel() // H, H, float(epsilon), 1 if use_per_token_quant else 0, _stream(input))
+
+
+def gelu_and_quant(out, input, scale_out, tmp):
+    """tanh-GELU + per-token int8 (``w8a8/act.cu:77-90``); writes out, scale_out, tmp."""
+    name = "gelu_and_quant"
+    dev = _check_cuda(name, out, input, scale_out, tmp)
+    _check_dtype(name, input, torch.float16)
+    _contig(name, out, input, scale_out, tmp)
+    d = input.shape[-1]
+    with _Dev(dev):
+        _lib.call("qvggt_gelu_quant", _ptr(out), _ptr(input), _ptr(scale_out), _ptr(tmp), input.numel() // d, d,
+                  _stream(input))
+
+
+def silu_and_mul(input):
+    raise NotImplementedError("silu_and_mul (SwiGLU) is not part of the VGGT path")
+
+
+# ---------------------------------------------------------------------- RoPE
+def fused_rope_with_pos_forward_func(input, freqs, transpose_output_memory: bool):
+    """Rotate-half RoPE with per-(b, s) angles (``fused_rope_with_pos.cu:122-164``).
+
+    input [s, b, h, d] fp16 (any strides), freqs fp32 [b, s, d2].  Returns a new
+    tensor [s, b, h, d]; with transpose_output_memory it is a transposed view of
+    a contiguous [b, s, h, d] buffer, as in the reference.
+    """
+    name = "fused_rope_with_pos_forward_func"
+    dev = _check_cuda(name, input, freqs)
+    _check_dtype(name, input, torch.float16)
+    _check_dtype(name, freqs, torch.float32)
+    s, b, h, d = input.shape
+    d2 = freqs.shape[-1]
+    freqs = freqs.contiguous()
+    if transpose_output_memory:
+        out = torch.empty(b, s, h, d, dtype=input.dtype, device=dev).transpose(0, 1)
+    else:
+        out = torch.empty(s, b, h, d, dtype=input.dtype, device=dev)
+    ist = (C.c_int64 * 4)(*input.stride())
+    ost = (C.c_int64 * 4)(*out.stride())
+    with _Dev(dev):
+        _lib.call("qvggt_rope_with_pos", _ptr(input), _ptr(freqs), _ptr(out), s, b, h, d, d2, ist, ost,
+                  _stream(input))
+    return out
+
+
+def rotary_embedding_neox(*args, **kw):
+    raise NotImplementedError("rotary_embedding_neox (1-D LLM RoPE) is not part of the VGGT path")
+
+
+def layernorm_forward_cuda(*args, **kw):
+    raise NotImplementedError("layernorm_forward_cuda (T5 RMSNorm) is not part of the VGGT path")
+
+
+def single_query_attention(*args, **kw):
+    raise NotImplementedError("single_query_attention (decode attention) is not part of the VGGT path")
+
+
+# ----------------------------------------------------------- new hot-path ops
+def layernorm(x, weight, bias, eps: float = 1e-6, out=None):
+    name = "layernorm"
+    dev = _check_cuda(name, x, weight, bias)
+    _contig(name, x, weight, bias)
+    H = x.shape[-1]
+    if out is None:
+        out = torch.empty_like(x)
+    with _Dev(dev):
+        _lib.call("qvggt_layernorm", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), x.numel() // H, H, float(eps),
+                  _stream(x))
+    return out
+
+
+def qkv_rope2d(qkv, heads: int, cos_tab, sin_tab, tokens_per_frame: int = 1374, patch_start: int = 5,
+               grid_w: int = 37, token_offset: int = 0, q_out=None, kv_out=None, qk_norm=None, eps: float = 1e-6):
+    """Split qkv [T, 3*C] into roped q [T, C] and [k roped | v] [T, 2*C]."""
+    name = "qkv_rope2d"
+    dev = _check_cuda(name, qkv, cos_tab, sin_tab)
+    _contig(name, qkv, cos_tab, sin_tab)
+    T = qkv.numel() // qkv.shape[-1]
+    Cd = qkv.shape[-1] // 3
+    if q_out is None:
+        q_out = torch.empty(T, Cd, dtype=torch.float16, device=dev)
+    if kv_out is None:
+        kv_out = torch.empty(T, 2 * Cd, dtype=torch.float16, device=dev)
+    qn = qk_norm if qk_norm is not None else (None, None, None, None)
+    with _Dev(dev):
+        _lib.call("qvggt_qkv_rope2d", _ptr(qkv), _ptr(q_out), _ptr(kv_out), T, heads, token_offset,
+                  tokens_per_frame, patch_start, grid_w, _ptr(cos_tab), _ptr(sin_tab), cos_tab.shape[0],
+                  1 if qk_norm is not None else 0, _ptr(qn[0]), _ptr(qn[1]), _ptr(qn[2]), _ptr(qn[3]), float(eps),
+                  _stream(qkv))
+    return q_out, kv_out
+
+
+def attention(q, kv, heads: int, batches: int, Lq: int, Lkv: int, out=None, k_col0: int | None = None,
+              v_col0: int | None = None):
+    """Flash attention (head_dim 64) over token-major q [batches*Lq, heads*64]
+    and kv [batches*Lkv, 2*heads*64] (= [k | v]).  Returns out [batches*Lq, heads*64]."""
+    name = "attention"
+    dev = _check_cuda(name, q, kv)
+    Cd = heads * 64
+    if out is None:
+        out = torch.empty(batches * Lq, Cd, dtype=torch.float16, device=dev)
+    k0 = 0 if k_col0 is None else k_col0
+    v0 = Cd if v_col0 is None else v_col0
+    with _Dev(dev):
+        _lib.call("qvggt_attention", _ptr(q), q.stride(0), _ptr(kv), kv.stride(0), k0, v0, _ptr(out), out.stride(0),
+                  batches, Lq, Lkv, heads, _stream(q))
+    return out

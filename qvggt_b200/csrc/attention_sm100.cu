@@ -1,0 +1,386 @@
+// Flash attention, head_dim 64, non-causal, for sm_100a (tcgen05 + TMEM + TMA).
+//
+// One CTA per (batch, head, block of 256 query rows) = two 128-row Q tiles
+// that share every K/V tile loaded into shared memory.  Per KV tile j of 128
+// keys:
+//   S_i = Q_i K_j^T        (tcgen05.mma, fp16 x fp16 -> fp32 in TMEM)
+//   P_i = exp2(S_i*c - m)  (softmax warpgroup i: one thread per query row,
+//                           tcgen05.ld of its S row, fp16 P written back to TMEM)
+//   O_i += P_i V_j         (tcgen05.mma with A = P read from TMEM, B = V from
+//                           shared memory in the MN-major 128-byte-swizzled layout)
+// The running maximum m is only raised when a row's new maximum exceeds it by
+// more than 2^8 (then O_i and the row sum are rescaled in place); P <= 256 fits
+// fp16 and the final O / l is exact either way.  While warpgroup 0 turns S_0
+// into P_0 the tensor core computes S_1 (and vice versa), so MMA and softmax
+// overlap.
+//
+// TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+//               O0 [384,448) O1 [448,512).
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 4..7 softmax WG 0,
+// 8..11 softmax WG 1.  All waits are bounded (common.cuh).
+#include "host.hpp"
+
+namespace qv {
+namespace {
+
+constexpr int KV_STAGES = 3;
+constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 fp16
+constexpr int THREADS = 384;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_S0 = 0, COL_P0 = 256, COL_O0 = 384;
+
+struct AttnSmem {
+  // offsets from a 1024-aligned base
+  static constexpr int Q0 = 0;
+  static constexpr int Q1 = Q0 + TILE_BYTES;
+  static constexpr int K = Q1 + TILE_BYTES;
+  static constexpr int V = K + KV_STAGES * TILE_BYTES;
+  static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
+  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_done[2], drain
+  static constexpr int NUM_BARS = 1 + 3 * KV_STAGES + 6 + 1;
+  static constexpr int MISC = BAR + NUM_BARS * 8;
+  static constexpr int TOTAL = MISC + 16 + 1024;
+};
+
+struct AttnArgs {
+  int heads, nqb, nkv;
+  long long Lq, Lkv;
+  __half* out;
+  long long o_stride;
+  float scale_log2;
+  Ctl ctl;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + AttnSmem::BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + KV_STAGES;
+  uint64_t* kv_empty = v_full + KV_STAGES;
+  uint64_t* s_full = kv_empty + KV_STAGES;  // [2]
+  uint64_t* p_full = s_full + 2;            // [2]
+  uint64_t* o_done = p_full + 2;            // [2]
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AttnSmem::MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + AttnSmem::MISC + 4);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qb = blockIdx.x % a.nqb;
+  const int h = (blockIdx.x / a.nqb) % a.heads;
+  const int b = blockIdx.x / (a.nqb * a.heads);
+  const long long q_row0 = (long long)b * a.Lq + (long long)qb * 256;   // first query row of this CTA
+  const long long kv_row0 = (long long)b * a.Lkv;
+  const int nkv = a.nkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      tma_load_3d(smem + AttnSmem::Q0, &tmQ, q_full, 0, h, (int)q_row0);
+      tma_load_3d(smem + AttnSmem::Q1, &tmQ, q_full, 0, h, (int)(q_row0 + 128));
+      int j = 0;
+      for (; j < nkv; ++j) {
+        const int st = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, a.ctl, ST_TIMEOUT_TMA_EMPTY)) break;
+        const int row = (int)(kv_row0 + (long long)j * 128);
+        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        tma_load_3d(smem + AttnSmem::K + st * TILE_BYTES, &tmK, &k_full[st], 0, h, row);
+        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+        tma_load_3d(smem + AttnSmem::V + st * TILE_BYTES, &tmV, &v_full[st], 0, h, row);
+      }
+      if (j < nkv) {
+        // aborted: let the loads already issued land before the CTA exits
+        mbar_wait_drain(q_full, 0, 200000000ull);
+        for (int jj = (j > KV_STAGES ? j - KV_STAGES : 0); jj < j; ++jj) {
+          const int st = jj % KV_STAGES;
+          mbar_wait_drain(&k_full[st], (jj / KV_STAGES) & 1, 200000000ull);
+          mbar_wait_drain(&v_full[st], (jj / KV_STAGES) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(128, 128);
+      constexpr uint32_t idesc_o = idesc_f16(128, 64, false, true);   // B = V, MN-major
+      const uint32_t q_addr[2] = {smem_u32(smem + AttnSmem::Q0), smem_u32(smem + AttnSmem::Q1)};
+      bool ok = mbar_wait(q_full, 0, abort_flag, a.ctl, ST_TIMEOUT_FULL);
+      auto issue_pv = [&](int i, int jj) {
+        const int st = jj % KV_STAGES;
+        const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_f16_ts(tmem + COL_O0 + i * 64, tmem + COL_P0 + i * 64 + k * 8, sdesc_sw128(v_addr + k * 2048), idesc_o,
+                     (jj > 0 || k > 0) ? 1u : 0u);
+        tc_commit(&o_done[i]);
+      };
+      int j = 0;
+      for (; ok && j < nkv; ++j) {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + AttnSmem::K + st * TILE_BYTES);
+        for (int i = 0; i < 2; ++i) {
+          if (j > 0) {
+            if (!mbar_wait(&p_full[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+            if (i == 0) {
+              const int sp = (j - 1) % KV_STAGES;
+              if (!mbar_wait(&v_full[sp], ((j - 1) / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
+                ok = false;
+                break;
+              }
+            }
+            tc_fence_after();
+            issue_pv(i, j - 1);
+            if (i == 1) tc_commit(&kv_empty[(j - 1) % KV_STAGES]);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f16_ss(tmem + COL_S0 + i * 128, sdesc_sw128(q_addr[i] + k * 32), sdesc_sw128(k_addr + k * 32),
+                       idesc_s, k > 0 ? 1u : 0u);
+          tc_commit(&s_full[i]);
+        }
+      }
+      if (ok && nkv > 0) {
+        const int jl = nkv - 1;
+        for (int i = 0; i < 2 && ok; ++i) {
+          if (!mbar_wait(&p_full[i], jl & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+          if (i == 0 &&
+              !mbar_wait(&v_full[jl % KV_STAGES], (jl / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(i, jl);
+        }
+        if (ok) tc_commit(&kv_empty[jl % KV_STAGES]);
+      }
+      if (!ok) {
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ softmax WG i
+    const int i = (warp - 4) / 4;
+    const int quarter = warp & 3;             // TMEM lane quarter
+    const int r = quarter * 32 + lane;        // row within the Q tile
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_base + COL_S0 + i * 128;
+    const uint32_t tP = tmem + lane_base + COL_P0 + i * 64;
+    const uint32_t tO = tmem + lane_base + COL_O0 + i * 64;
+    const float c = a.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait_warp(&s_full[i], j & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+      tc_fence_after();
+      const long long rem = a.Lkv - (long long)j * 128;
+      const int valid = rem >= 128 ? 128 : (int)rem;
+      // pass 1: row maximum of the raw scores
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(tS + cc * 32, v);
+        tmem_ld_wait();
+        if (valid == 128) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (cc * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
+        }
+      }
+      const float m_new = fmaxf(m_used, mx * c);
+      const bool need = m_new > m_used + 8.0f;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_target = need ? m_new : m_used;
+        const float alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_target);
+        if (j > 0) {
+          if (!mbar_wait_warp(&o_done[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t v[16];
+            tmem_ld16(tO + cc * 16, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st16(tO + cc * 16, v);
+          }
+          tmem_st_wait();
+        }
+        l *= alpha;
+        m_used = m_target;
+      }
+      // pass 2: P = exp2(S*c - m), row sum, fp16 P into TMEM
+      const float neg_m = -m_used;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(tS + cc * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float p0 = ex2(fmaf(__uint_as_float(v[2 * e]), c, neg_m));
+          float p1 = ex2(fmaf(__uint_as_float(v[2 * e + 1]), c, neg_m));
+          if (valid < 128) {
+            if (cc * 32 + 2 * e >= valid) p0 = 0.f;
+            if (cc * 32 + 2 * e + 1 >= valid) p1 = 0.f;
+          }
+          l += p0 + p1;
+          pk[e] = pack_half2(p0, p1);
+        }
+        tmem_st16(tP + cc * 16, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[i]);
+    }
+    if (ok && nkv > 0) {
+      if (mbar_wait_warp(&o_done[i], (nkv - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) {
+        tc_fence_after();
+        const long long qr = (long long)qb * 256 + i * 128 + r;   // row within the batch
+        const float inv = 1.f / l;
+        __half* dst = a.out + (q_row0 + i * 128 + r) * a.o_stride + h * 64;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[16];
+          tmem_ld16(tO + cc * 16, v);
+          tmem_ld_wait();
+          uint32_t o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            o[e] = pack_half2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
+          if (qr < a.Lq) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 16);
+            d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+}  // namespace qv
+
+using namespace qv;
+
+extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                               int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
+                               int32_t heads, void* stream) {
+  if (batches < 0 || Lq < 0 || heads <= 0) return set_error(QVGGT_ERR_INVALID, "attention: bad shape");
+  if (Lkv <= 0) return set_error(QVGGT_ERR_INVALID, "attention: Lkv must be > 0");
+  if (q_stride % 8 || kv_stride % 8 || o_stride % 8 || k_col0 % 8 || v_col0 % 8)
+    return set_error(QVGGT_ERR_ALIGN, "attention: strides and column offsets must be multiples of 8");
+  if (!aligned16(q) || !aligned16(kv) || !aligned16(out))
+    return set_error(QVGGT_ERR_ALIGN, "attention: tensors must be 16-byte aligned");
+  if (q_stride < heads * 64 || o_stride < heads * 64 || kv_stride < k_col0 + heads * 64 ||
+      kv_stride < v_col0 + heads * 64)
+    return set_error(QVGGT_ERR_INVALID, "attention: strides too small for the heads");
+  const long long q_rows = batches * Lq, kv_rows = batches * Lkv;
+  if (q_rows + 256 > 2147483647LL || kv_rows > 2147483647LL)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "attention: too many rows for 32-bit TMA coordinates");
+  if (batches == 0 || Lq == 0) return QVGGT_OK;
+  const DeviceInfo& di = device_info();
+  if (AttnSmem::TOTAL > di.max_smem_optin)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "attention: shared memory %d > %d", AttnSmem::TOTAL, di.max_smem_optin);
+
+  CUtensorMap tmQ, tmK, tmV;
+  {
+    const uint64_t dims[3] = {64, (uint64_t)heads, (uint64_t)q_rows};
+    const uint64_t strides[2] = {128, (uint64_t)q_stride * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    int rc = encode_tmap(&tmQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {64, (uint64_t)heads, (uint64_t)kv_rows};
+    const uint64_t strides[2] = {128, (uint64_t)kv_stride * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    const __half* kb = static_cast<const __half*>(kv) + k_col0;
+    const __half* vb = static_cast<const __half*>(kv) + v_col0;
+    int rc = encode_tmap(&tmK, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, kb, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = encode_tmap(&tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vb, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  AttnArgs a;
+  a.heads = heads;
+  a.nqb = (int)((Lq + 255) / 256);
+  a.nkv = (int)((Lkv + 127) / 128);
+  a.Lq = Lq;
+  a.Lkv = Lkv;
+  a.out = static_cast<__half*>(out);
+  a.o_stride = o_stride;
+  a.scale_log2 = 0.125f * 1.4426950408889634f;
+  a.ctl = make_ctl();
+  const long long grid = (long long)a.nqb * heads * batches;
+  if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
+  static bool attr_set[64] = {};
+  if (di.device < 64 && !attr_set[di.device]) {
+    int rc = check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             AttnSmem::TOTAL),
+                        "cudaFuncSetAttribute(attention)");
+    if (rc) return rc;
+    attr_set[di.device] = true;
+  }
+  attn_fwd_kernel<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK, tmV, a);
+  int rc = check_cuda(cudaGetLastError(), "attention launch");
+  if (!rc) count_launch(1);
+  return rc;
+}

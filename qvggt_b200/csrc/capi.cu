@@ -1,0 +1,235 @@
+// C ABI: library state (errors, device status word, wait budget, tensor-map
+// encoding) and the GEMM entry points.  The other kernels' entry points live
+// beside their kernels.
+#include <atomic>
+#include <cstring>
+#include <mutex>
+
+#include "gemm_sm100.cuh"
+#include "host.hpp"
+
+namespace qv {
+
+namespace {
+thread_local char g_errmsg[512] = {0};
+std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+std::atomic<uint64_t> g_launches{0};
+DeviceInfo g_dev[64];
+uint32_t* g_status_ptr[64] = {};
+std::mutex g_mu;
+}  // namespace
+
+// The device status word.  One per device (every device that loads the
+// library holds its own copy); kernels receive its address in their Ctl.
+__device__ uint32_t g_device_status[4];
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_errmsg, sizeof(g_errmsg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return QVGGT_OK;
+  return set_error(QVGGT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+const DeviceInfo& device_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  DeviceInfo& d = g_dev[dev];
+  if (d.device != dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (d.device != dev) {
+      cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+      cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+      cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+      cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+      d.device = dev;
+    }
+  }
+  return d;
+}
+
+static uint32_t* status_ptr() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!g_status_ptr[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_status_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess) g_status_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+  }
+  return g_status_ptr[dev];
+}
+
+Ctl make_ctl() {
+  Ctl c;
+  c.status = status_ptr();
+  c.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+  return c;
+}
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+      return set_error(QVGGT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) s[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(QVGGT_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QVGGT_OK;
+}
+
+// Self-test kernel: one bounded wait on a barrier nothing arrives on.
+__global__ void selftest_wait_kernel(Ctl ctl) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, ctl, ST_TIMEOUT_SELFTEST);
+  __syncthreads();
+}
+
+}  // namespace qv
+
+using namespace qv;
+
+extern "C" {
+
+int qvggt_version(void) { return 100; }
+
+const char* qvggt_last_error(void) { return g_errmsg; }
+
+uint64_t qvggt_launch_count(void) { return g_launches.load(); }
+
+int qvggt_set_wait_timeout_ns(uint64_t ns) {
+  if (ns == 0) return set_error(QVGGT_ERR_INVALID, "timeout must be > 0");
+  g_timeout_ns.store(ns);
+  return QVGGT_OK;
+}
+
+int qvggt_device_status(uint32_t* status_out, int clear) {
+  int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (rc) return rc;
+  uint32_t v[4] = {0, 0, 0, 0};
+  rc = check_cuda(cudaMemcpyFromSymbol(v, g_device_status, sizeof(v)), "read status");
+  if (rc) return rc;
+  if (status_out) *status_out = v[0];
+  if (clear) {
+    uint32_t z[4] = {0, 0, 0, 0};
+    rc = check_cuda(cudaMemcpyToSymbol(g_device_status, z, sizeof(z)), "clear status");
+    if (rc) return rc;
+  }
+  return QVGGT_OK;
+}
+
+int qvggt_selftest_wait_timeout(uint64_t timeout_ns, uint32_t* status_out) {
+  uint32_t st = 0;
+  int rc = qvggt_device_status(&st, 1);
+  if (rc) return rc;
+  Ctl ctl = make_ctl();
+  ctl.timeout_ns = timeout_ns;
+  selftest_wait_kernel<<<1, 32>>>(ctl);
+  count_launch(1);
+  rc = check_cuda(cudaGetLastError(), "selftest launch");
+  if (rc) return rc;
+  rc = qvggt_device_status(&st, 1);
+  if (rc) return rc;
+  if (status_out) *status_out = st;
+  return st == ST_TIMEOUT_SELFTEST ? QVGGT_ERR_TIMEOUT : QVGGT_OK;
+}
+
+int qvggt_w4a16_gemm(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                     const void* bias, void* out, int64_t M, int64_t N, int64_t K, int64_t gpad,
+                     int32_t group_size, void* stream) {
+  return qvggt_w4a16_linear_ex(in_feats, K, qweight, scales, scaled_zeros, bias, out, N, M, N, K, gpad, group_size,
+                               0, nullptr, 0, nullptr, stream);
+}
+
+int qvggt_w4a16_linear_ex(const void* in_feats, int64_t lda, const void* qweight, const void* scales,
+                          const void* scaled_zeros, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
+                          int64_t K, int64_t gpad, int32_t group_size, int32_t act, const void* resid,
+                          int64_t ldr, const void* gamma, void* stream) {
+  GemmLaunch L;
+  L.mode = B_W4;
+  L.epi = resid ? EPI_RESID : (act == 1 ? EPI_GELU : EPI_STORE);
+  if (resid && act) return set_error(QVGGT_ERR_INVALID, "act and residual are exclusive");
+  if (resid && resid != out) return set_error(QVGGT_ERR_INVALID, "residual epilogue updates in place: out == resid");
+  if (lda % 8 || ldo % 8 || (resid && ldr % 8)) return set_error(QVGGT_ERR_ALIGN, "strides must be multiples of 8");
+  L.a = in_feats; L.lda = lda; L.b = qweight; L.scales = scales; L.zeros = scaled_zeros; L.gpad = gpad;
+  L.group_size = group_size; L.bias = bias; L.out = out; L.ldo = ldo; L.resid = resid; L.ldr = ldr;
+  L.gamma = gamma; L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
+int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, const void* bias, void* out,
+                        int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
+                        const void* gamma, void* stream) {
+  GemmLaunch L;
+  L.mode = B_F16;
+  L.epi = resid ? EPI_RESID : (act == 1 ? EPI_GELU : EPI_STORE);
+  if (resid && act) return set_error(QVGGT_ERR_INVALID, "act and residual are exclusive");
+  if (resid && resid != out) return set_error(QVGGT_ERR_INVALID, "residual epilogue updates in place: out == resid");
+  if (lda % 8 || ldo % 8 || (resid && ldr % 8)) return set_error(QVGGT_ERR_ALIGN, "strides must be multiples of 8");
+  L.a = in_feats; L.lda = lda; L.b = weight; L.bias = bias; L.out = out; L.ldo = ldo; L.resid = resid;
+  L.ldr = ldr; L.gamma = gamma; L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
+int qvggt_w8a8_gemm(const int8_t* in, const int8_t* w, const void* wscales, const void* ascales, const void* bias,
+                    void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+  GemmLaunch L;
+  L.mode = B_I8;
+  L.epi = EPI_STORE;
+  L.a = in; L.lda = K; L.b = w; L.bias = bias; L.out = out; L.ldo = N; L.wscale = wscales; L.ascale = ascales;
+  L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
+int qvggt_i8_gemm_i32(const int8_t* in, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                      void* stream) {
+  GemmLaunch L;
+  L.mode = B_I8;
+  L.epi = EPI_I32;
+  L.a = in; L.lda = K; L.b = w; L.out = acc; L.ldo = N;
+  L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,508 @@
+// Persistent tcgen05 GEMM for sm_100a: C[M, N] = A[M, K] . B[N, K]^T with a
+// fused epilogue, in three operand modes:
+//
+//   B_W4  : A fp16, B = AWQ-packed int4 (qweight int16 [N/4, K]) with fp16
+//           per-group scales / scaled zeros [Gpad, N].  TMA brings the packed
+//           words and the group's scales into shared memory; dequantisation
+//           warps turn them into fp16 in the 128-byte-swizzled K-major layout
+//           the tensor core reads; fp32 accumulation in TMEM.
+//   B_F16 : A fp16, B fp16 [N, K] (dense, e.g. the unquantised patch embed).
+//   B_I8  : A int8 [M, K], B int8 [N, K], int32 accumulation in TMEM, and the
+//           per-token x per-channel rescale epilogue of the reference W8A8 GEMM.
+//
+// Tile 128 x BN x (128 bytes of K), one CTA per SM, static persistent tile
+// schedule (m-major so CTAs running together share A rows in L2), two TMEM
+// accumulators so the epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 4..7 = epilogue (TMEM lane quarters 0..3), warps 8.. = dequantisation
+// (B_W4 only).  All inter-role waits are bounded (see common.cuh).
+#include "gemm_sm100.cuh"
+#include "host.hpp"
+
+namespace qv {
+namespace {
+
+constexpr int BM = 128;
+constexpr int KB_BYTES = 128;  // bytes of K per k-block (64 fp16 or 128 int8)
+
+template <int BN, int MODE>
+struct Cfg {
+  static constexpr int NS = (MODE == B_W4) ? (BN == 256 ? 4 : 6) : (BN == 256 ? 4 : 6);
+  static constexpr int ND = (MODE == B_W4) ? 3 : 0;
+  static constexpr int A_BYTES = BM * KB_BYTES;                           // 16 KB
+  static constexpr int B_BYTES = BN * KB_BYTES;                           // fp16/int8 operand tile
+  static constexpr int BQ_BYTES = (MODE == B_W4) ? (BN / 4) * KB_BYTES : 0; // packed int4 tile
+  static constexpr int SZ_BYTES = (MODE == B_W4) ? 2 * BN * 2 : 0;         // scales + zeros
+  static constexpr int NUM_DQ_WARPS = (MODE == B_W4) ? BN / 32 : 0;
+  static constexpr int THREADS = 256 + NUM_DQ_WARPS * 32;
+  // shared memory carve-up (offsets from a 1024-aligned base)
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + NS * A_BYTES;                      // B_F16/B_I8 operand stages
+  static constexpr int OFF_BQ = OFF_A + NS * A_BYTES;                     // B_W4 packed stages
+  static constexpr int OFF_D = (MODE == B_W4) ? OFF_BQ + NS * BQ_BYTES : OFF_B + NS * B_BYTES;
+  static constexpr int OFF_SZ = OFF_D + ND * B_BYTES;
+  static constexpr int OFF_BAR = ((OFF_SZ + NS * SZ_BYTES) + 15) / 16 * 16;
+  static constexpr int NUM_BARS = 4 * NS + 2 * ND + 4 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int n_blocks, num_tiles, num_kb;
+  int group_size;
+  int epi;
+  const __half* bias;
+  __half* out;
+  long long ldo;
+  const __half* resid;
+  long long ldr;
+  const __half* gamma;
+  const __half* wscale;
+  const __half* ascale;
+  Ctl ctl;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+// Epilogue for 16 consecutive columns of one row held as fp32 (or s32) bits.
+template <int MODE>
+__device__ __forceinline__ void epilogue16(const GemmArgs& g, int row, int col, const uint32_t (&r)[16]) {
+  float y[16];
+  if constexpr (MODE == B_I8) {
+    if (g.epi == EPI_I32) {
+      uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(g.out) + (long long)row * g.ldo + col);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) op[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+      return;
+    }
+    const float as = __half2float(g.ascale[row]);
+    const uint4* wsp = reinterpret_cast<const uint4*>(g.wscale + col);
+    uint32_t wsu[8];
+    *reinterpret_cast<uint4*>(&wsu[0]) = __ldg(wsp);
+    *reinterpret_cast<uint4*>(&wsu[4]) = __ldg(wsp + 1);
+    if (g.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col);
+      uint32_t bu[8];
+      *reinterpret_cast<uint4*>(&bu[0]) = __ldg(bp);
+      *reinterpret_cast<uint4*>(&bu[4]) = __ldg(bp + 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 ws = unpack_half2(wsu[i]);
+        float2 b = unpack_half2(bu[i]);
+        // (acc * ws) * as + bias, contracted (w8a8_gemm_cuda.cu:551-556)
+        y[2 * i] = __fmaf_rn(__fmul_rn(__int2float_rn((int)r[2 * i]), ws.x), as, b.x);
+        y[2 * i + 1] = __fmaf_rn(__fmul_rn(__int2float_rn((int)r[2 * i + 1]), ws.y), as, b.y);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 ws = unpack_half2(wsu[i]);
+        // acc * (ws * as) (w8a8_gemm_cuda.cu:868-873)
+        y[2 * i] = __fmul_rn(__int2float_rn((int)r[2 * i]), __fmul_rn(ws.x, as));
+        y[2 * i + 1] = __fmul_rn(__int2float_rn((int)r[2 * i + 1]), __fmul_rn(ws.y, as));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = round_f16(__uint_as_float(r[i]));
+    if (g.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col);
+      uint32_t bu[8];
+      *reinterpret_cast<uint4*>(&bu[0]) = __ldg(bp);
+      *reinterpret_cast<uint4*>(&bu[4]) = __ldg(bp + 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 b = unpack_half2(bu[i]);
+        y[2 * i] = round_f16(y[2 * i] + b.x);
+        y[2 * i + 1] = round_f16(y[2 * i + 1] + b.y);
+      }
+    }
+    if (g.epi == EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) y[i] = gelu_erf(y[i]);
+    } else if (g.epi == EPI_RESID) {
+      const uint4* gp = reinterpret_cast<const uint4*>(g.gamma + col);
+      const uint4* rp = reinterpret_cast<const uint4*>(g.resid + (long long)row * g.ldr + col);
+      uint32_t gu[8], ru[8];
+      *reinterpret_cast<uint4*>(&gu[0]) = __ldg(gp);
+      *reinterpret_cast<uint4*>(&gu[4]) = __ldg(gp + 1);
+      *reinterpret_cast<uint4*>(&ru[0]) = rp[0];
+      *reinterpret_cast<uint4*>(&ru[4]) = rp[1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 gm = unpack_half2(gu[i]);
+        float2 x = unpack_half2(ru[i]);
+        y[2 * i] = x.x + round_f16(y[2 * i] * gm.x);
+        y[2 * i + 1] = x.y + round_f16(y[2 * i + 1] * gm.y);
+      }
+    }
+  }
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = pack_half2(y[2 * i], y[2 * i + 1]);
+  uint4* op = reinterpret_cast<uint4*>(g.out + (long long)row * g.ldo + col);
+  op[0] = *reinterpret_cast<uint4*>(&o[0]);
+  op[1] = *reinterpret_cast<uint4*>(&o[4]);
+}
+
+// Dequantise one 16-byte chunk (4 u32 = 32 nibbles of one channel, covering
+// 32 consecutive k) into four 16-byte fp16 chunks (8 consecutive k each).
+//
+// Word w of a channel's 16-word segment holds, in nibble j, k = 32*(w/8) + w%8 + 8j
+// (relative to its 64-wide k-chunk).  The u32 formed by words (2u, 2u+1)
+// therefore holds the k pair (b, b+1), b = 2u (mod 8), in nibbles (j, j+4) for
+// each j, i.e. in the 16-bit halves of (x >> 4j) & 0x000F000F.  OR-ing the
+// exponent pattern 0x6400 makes each half the fp16 value 1024 + q exactly;
+// subtracting 1024 leaves the exact integer q; one fused multiply-add applies
+// the group scale and scaled zero (rounded once, as the reference's __hfma2).
+__device__ __forceinline__ void dequant_chunk(const uint32_t (&x)[4], __half2 s2, __half2 z2, uint4 (&out)[4]) {
+  const __half2 magic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint32_t t;
+      const uint32_t src = x[u] >> (4 * q);
+      asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(0x64006400u));
+      __half2 hq = __hsub2(*reinterpret_cast<__half2*>(&t), magic);
+      __half2 w = __hfma2(hq, s2, z2);
+      o[u] = *reinterpret_cast<uint32_t*>(&w);
+    }
+    out[q] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ, GemmArgs g) {
+  using C = Cfg<BN, MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full_a = bars;                 // [NS] TMA -> MMA (A, and B for dense modes)
+  uint64_t* empty_a = bars + C::NS;        // [NS] MMA -> TMA
+  uint64_t* full_b = bars + 2 * C::NS;     // [NS] TMA -> dequant (B_W4)
+  uint64_t* empty_b = bars + 3 * C::NS;    // [NS] dequant -> TMA (B_W4)
+  uint64_t* full_d = bars + 4 * C::NS;     // [ND] dequant -> MMA
+  uint64_t* empty_d = full_d + C::ND;      // [ND] MMA -> dequant
+  uint64_t* tmem_full = empty_d + C::ND;   // [2] MMA -> epilogue
+  uint64_t* tmem_empty = tmem_full + 2;    // [2] epilogue -> MMA
+  uint64_t* drain_bar = tmem_empty + 2;    // MMA drain on abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+      mbar_init(&full_b[i], 1);
+      mbar_init(&empty_b[i], C::NUM_DQ_WARPS > 0 ? C::NUM_DQ_WARPS : 1);
+    }
+    for (int i = 0; i < C::ND; ++i) {
+      mbar_init(&full_d[i], C::NUM_DQ_WARPS);
+      mbar_init(&empty_d[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tmem_full[i], 1);
+      mbar_init(&tmem_empty[i], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if constexpr (MODE == B_W4) {
+      tma_prefetch_desc(&tmS);
+      tma_prefetch_desc(&tmZ);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_kb = g.num_kb;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile / g.n_blocks, n_blk = tile % g.n_blocks;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % C::NS;
+          const uint32_t ph = (it / C::NS) & 1;
+          if (!mbar_wait(&empty_a[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+          uint8_t* sa = smem + C::OFF_A + s * C::A_BYTES;
+          if constexpr (MODE == B_W4) {
+            mbar_arrive_expect_tx(&full_a[s], C::A_BYTES);
+            tma_load_2d(sa, &tmA, &full_a[s], kb * 64, m_blk * BM);
+            if (!mbar_wait(&empty_b[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ++it; ok = false; break; }
+            uint8_t* sq = smem + C::OFF_BQ + s * C::BQ_BYTES;
+            uint8_t* ssz = smem + C::OFF_SZ + s * C::SZ_BYTES;
+            const int grp = (kb * 64) / g.group_size;
+            mbar_arrive_expect_tx(&full_b[s], C::BQ_BYTES + C::SZ_BYTES);
+            tma_load_2d(sq, &tmB, &full_b[s], kb * 64, n_blk * (BN / 4));
+            tma_load_2d(ssz, &tmS, &full_b[s], n_blk * BN, grp);
+            tma_load_2d(ssz + BN * 2, &tmZ, &full_b[s], n_blk * BN, grp);
+          } else {
+            uint8_t* sb = smem + C::OFF_B + s * C::B_BYTES;
+            mbar_arrive_expect_tx(&full_a[s], C::A_BYTES + C::B_BYTES);
+            tma_load_2d(sa, &tmA, &full_a[s], kb * KB_BYTES / (MODE == B_I8 ? 1 : 2), m_blk * BM);
+            tma_load_2d(sb, &tmB, &full_a[s], kb * KB_BYTES / (MODE == B_I8 ? 1 : 2), n_blk * BN);
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) for every load already issued to land.
+        const uint32_t issued = it;
+        for (int s = 0; s < C::NS; ++s) {
+          const uint32_t cnt = issued > (uint32_t)s ? (issued - 1 - s) / C::NS + 1 : 0;
+          if (cnt == 0) continue;
+          mbar_wait_drain(&full_a[s], (cnt - 1) & 1, 200000000ull);
+          if constexpr (MODE == B_W4) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = (MODE == B_I8) ? idesc_i8(BM, BN) : idesc_f16(BM, BN);
+      uint32_t it = 0;
+      int t_local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.num_tiles && ok; tile += gridDim.x, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t aph = (t_local >> 1) & 1;
+        if (!mbar_wait(&tmem_empty[acc], aph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMEM)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % C::NS;
+          const uint32_t ph = (it / C::NS) & 1;
+          if (!mbar_wait(&full_a[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+          const uint8_t* sb;
+          int d = 0;
+          if constexpr (MODE == B_W4) {
+            d = it % C::ND;
+            const uint32_t dph = (it / C::ND) & 1;
+            if (!mbar_wait(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+            sb = smem + C::OFF_D + d * C::B_BYTES;
+          } else {
+            sb = smem + C::OFF_B + s * C::B_BYTES;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + C::OFF_A + s * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sb);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = sdesc_sw128(a_addr + k * 32);
+            const uint64_t bd = sdesc_sw128(b_addr + k * 32);
+            if constexpr (MODE == B_I8)
+              mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          tc_commit(&empty_a[s]);
+          if constexpr (MODE == B_W4) tc_commit(&empty_d[d]);
+        }
+        if (!ok) break;
+        tc_commit(&tmem_full[acc]);
+      }
+      if (!ok) {
+        tc_commit(drain_bar);
+        mbar_wait_drain(drain_bar, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp - 4;  // TMEM lane quarter
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x, ++t_local) {
+      const int m_blk = tile / g.n_blocks, n_blk = tile % g.n_blocks;
+      const int acc = t_local & 1;
+      const uint32_t aph = (t_local >> 1) & 1;
+      if (!mbar_wait_warp(&tmem_full[acc], aph, abort_flag, g.ctl, ST_TIMEOUT_TMEM)) break;
+      tc_fence_after();
+      const int row = m_blk * BM + q * 32 + lane;
+      const uint32_t tbase = tmem_addr(tmem_base, q * 32, acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c * 16, r);
+        tmem_ld_wait();
+        if (row < g.M) epilogue16<MODE>(g, row, n_blk * BN + c * 16, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dequantisation
+    if constexpr (MODE == B_W4) {
+      const int n = threadIdx.x - 256;  // channel within the tile, 0..BN-1
+      const int grow = n >> 2;          // packed row within the tile
+      const int ci = n & 3;             // channel within the packed row
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < g.num_tiles; tile += gridDim.x) {
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % C::NS;
+          const uint32_t ph = (it / C::NS) & 1;
+          if (!mbar_wait_warp(&full_b[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+          const uint8_t* sq = smem + C::OFF_BQ + s * C::BQ_BYTES + grow * 128;
+          const __half* ssz = reinterpret_cast<const __half*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
+          uint32_t x0[4], x1[4];
+          *reinterpret_cast<uint4*>(x0) = *reinterpret_cast<const uint4*>(sq + (((2 * ci) ^ (grow & 7)) * 16));
+          *reinterpret_cast<uint4*>(x1) = *reinterpret_cast<const uint4*>(sq + (((2 * ci + 1) ^ (grow & 7)) * 16));
+          const __half2 s2 = __half2half2(ssz[n]);
+          const __half2 z2 = __half2half2(ssz[BN + n]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty_b[s]);
+          const int d = it % C::ND;
+          const uint32_t dph = (it / C::ND) & 1;
+          if (!mbar_wait_warp(&empty_d[d], dph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+          uint8_t* drow = smem + C::OFF_D + d * C::B_BYTES + n * 128;
+          uint4 o[4];
+          dequant_chunk(x0, s2, z2, o);
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + ((qq ^ (n & 7)) * 16)) = o[qq];
+          dequant_chunk(x1, s2, z2, o);
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full_d[d]);
+        }
+        if (!ok) break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int BN, int MODE>
+int launch_gemm(const GemmLaunch& L) {
+  using C = Cfg<BN, MODE>;
+  const DeviceInfo& di = device_info();
+  if (C::SMEM > di.max_smem_optin)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: %d B shared memory exceeds the device limit %d", C::SMEM,
+                     di.max_smem_optin);
+  CUtensorMap tmA, tmB, tmS, tmZ;
+  int rc;
+  if constexpr (MODE == B_I8) {
+    rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.a, L.K, L.M, L.lda, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.b, L.K, L.N, L.K, 128, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    tmS = tmB;
+    tmZ = tmB;
+  } else {
+    rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.a, L.K, L.M, L.lda * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if constexpr (MODE == B_W4) {
+      rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT16, L.b, L.K, L.N / 4, L.K * 2, 64, BN / 4,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      rc = tmap_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.scales, L.N, L.gpad, L.N * 2, BN, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+      rc = tmap_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.zeros, L.N, L.gpad, L.N * 2, BN, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+    } else {
+      rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.b, L.K, L.N, L.K * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      tmS = tmB;
+      tmZ = tmB;
+    }
+  }
+  GemmArgs g;
+  g.M = (int)L.M;
+  g.N = (int)L.N;
+  g.K = (int)L.K;
+  g.n_blocks = (int)(L.N / BN);
+  const int m_blocks = (int)((L.M + BM - 1) / BM);
+  g.num_tiles = m_blocks * g.n_blocks;
+  g.num_kb = (int)(L.K * (MODE == B_I8 ? 1 : 2) / KB_BYTES);
+  g.group_size = L.group_size;
+  g.epi = L.epi;
+  g.bias = reinterpret_cast<const __half*>(L.bias);
+  g.out = reinterpret_cast<__half*>(L.out);
+  g.ldo = L.ldo;
+  g.resid = reinterpret_cast<const __half*>(L.resid);
+  g.ldr = L.ldr;
+  g.gamma = reinterpret_cast<const __half*>(L.gamma);
+  g.wscale = reinterpret_cast<const __half*>(L.wscale);
+  g.ascale = reinterpret_cast<const __half*>(L.ascale);
+  g.ctl = make_ctl();
+  if (g.num_tiles == 0) return QVGGT_OK;
+
+  auto kfn = gemm_kernel<BN, MODE>;
+  static bool attr_set[16] = {};
+  const int dev = di.device;
+  if (dev < 16 && !attr_set[dev]) {
+    rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                    "cudaFuncSetAttribute(gemm)");
+    if (rc) return rc;
+    attr_set[dev] = true;
+  }
+  const int grid = g.num_tiles < di.num_sms ? g.num_tiles : di.num_sms;
+  kfn<<<grid, C::THREADS, C::SMEM, L.stream>>>(tmA, tmB, tmS, tmZ, g);
+  return check_cuda(cudaGetLastError(), "gemm launch");
+}
+
+}  // namespace
+
+int gemm_launch(const GemmLaunch& L) {
+  // Shape and layout checks shared by all modes.
+  if (L.M < 0 || L.N <= 0 || L.K <= 0) return set_error(QVGGT_ERR_INVALID, "gemm: bad shape M=%lld N=%lld K=%lld",
+                                                        (long long)L.M, (long long)L.N, (long long)L.K);
+  if (L.N % 128 != 0) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: N=%lld must be a multiple of 128", (long long)L.N);
+  const int kmul = (L.mode == B_I8) ? 128 : 64;
+  if (L.K % kmul != 0)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: K=%lld must be a multiple of %d", (long long)L.K, kmul);
+  if (!aligned16(L.a) || !aligned16(L.b) || !aligned16(L.out) || (L.bias && !aligned16(L.bias)))
+    return set_error(QVGGT_ERR_ALIGN, "gemm: operands must be 16-byte aligned");
+  if (L.mode == B_W4) {
+    if (L.group_size <= 0 || L.group_size % 64 != 0 || L.K % L.group_size != 0)
+      return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: group_size=%d must be a multiple of 64 dividing K=%lld",
+                       L.group_size, (long long)L.K);
+    if (L.gpad < L.K / L.group_size) return set_error(QVGGT_ERR_INVALID, "gemm: scale table has too few groups");
+    if (!aligned16(L.scales) || !aligned16(L.zeros)) return set_error(QVGGT_ERR_ALIGN, "gemm: scales not aligned");
+  }
+  if (L.epi == EPI_RESID && (!L.resid || !L.gamma)) return set_error(QVGGT_ERR_INVALID, "gemm: residual needs resid+gamma");
+  if (L.mode == B_I8 && L.epi != EPI_I32 && (!L.wscale || !L.ascale)) return set_error(QVGGT_ERR_INVALID, "gemm: w8a8 needs scales");
+  if (L.M == 0) return QVGGT_OK;
+
+  const bool bn256 = (L.N % 256 == 0) && !L.force_bn128;
+  switch (L.mode) {
+    case B_W4: return bn256 ? launch_gemm<256, B_W4>(L) : launch_gemm<128, B_W4>(L);
+    case B_F16: return bn256 ? launch_gemm<256, B_F16>(L) : launch_gemm<128, B_F16>(L);
+    case B_I8: return bn256 ? launch_gemm<256, B_I8>(L) : launch_gemm<128, B_I8>(L);
+  }
+  return set_error(QVGGT_ERR_INVALID, "gemm: bad mode");
+}
+
+}  // namespace qv

@@ -1,0 +1,37 @@
+// Internal launch description of the tcgen05 GEMM (see gemm_sm100.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qv {
+
+enum GemmMode { B_W4 = 0, B_F16 = 1, B_I8 = 2 };
+enum GemmEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_I32 = 3 };
+
+struct GemmLaunch {
+  int mode = B_W4;
+  int epi = EPI_STORE;
+  const void* a = nullptr;   // [M, lda] fp16 (or int8 for B_I8)
+  long long lda = 0;         // elements
+  const void* b = nullptr;   // B_W4: qweight int16 [N/4, K]; B_F16: fp16 [N, K]; B_I8: int8 [N, K]
+  const void* scales = nullptr;  // B_W4: fp16 [gpad, N]
+  const void* zeros = nullptr;   // B_W4: fp16 [gpad, N] (scaled zeros)
+  long long gpad = 0;
+  int group_size = 128;
+  const void* bias = nullptr;    // fp16 [N] or null
+  void* out = nullptr;           // fp16 [M, ldo] (int32 for EPI_I32)
+  long long ldo = 0;
+  const void* resid = nullptr;   // EPI_RESID: fp16 [M, ldr] (may alias out)
+  long long ldr = 0;
+  const void* gamma = nullptr;   // EPI_RESID: fp16 [N] LayerScale
+  const void* wscale = nullptr;  // B_I8: fp16 [N]
+  const void* ascale = nullptr;  // B_I8: fp16 [M]
+  long long M = 0, N = 0, K = 0;
+  bool force_bn128 = false;
+  cudaStream_t stream = nullptr;
+};
+
+int gemm_launch(const GemmLaunch& L);
+
+}  // namespace qv

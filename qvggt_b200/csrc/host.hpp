@@ -1,0 +1,55 @@
+// Host-side helpers shared by the C-ABI launchers: error reporting, device
+// properties, the device status word, and TMA tensor-map encoding.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/qvggt_b200.h"
+#include "common.cuh"
+
+namespace qv {
+
+// Records a human-readable message for qvggt_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+// Adds n to the library's launch counter (qvggt_launch_count).
+void count_launch(int n);
+// Maps a CUDA error to QVGGT_ERR_CUDA with the CUDA message; 0 if success.
+int check_cuda(cudaError_t e, const char* what);
+
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+// Properties of the current device (cached per device).
+const DeviceInfo& device_info();
+
+// Device status word of the current device (library-owned; see capi.cu) and
+// the wait budget every bounded device-side wait uses.
+Ctl make_ctl();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes /* rank-1 entries */, const uint32_t* box,
+                CUtensorMapSwizzle swizzle);
+
+// 2-D row-major [rows, cols] tile map: box = box_cols x box_rows.
+inline int tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t cols, uint64_t rows,
+                   uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  uint64_t dims[2] = {cols, rows};
+  uint64_t strides[1] = {row_stride_bytes};
+  uint32_t box[2] = {box_cols, box_rows};
+  return encode_tmap(map, dtype, 2, base, dims, strides, box, sw);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace qv
