@@ -170,6 +170,27 @@ int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_
                     int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
                     int32_t heads, void* stream);
 
+/* ---------------------------------------------------------- patch embed */
+
+/* images fp16 [S, 3, H, W] (pixels in [0, 1]) -> patches fp16
+ * [S*(H/patch)*(W/patch), k_pad]: column c*patch^2 + ky*patch + kx holds
+ * half(half(x - mean[c]) / std[c]), columns >= 3*patch^2 are zero.  Turns the
+ * patch-embed convolution of the DINOv2 front into a GEMM.  No reference
+ * counterpart (the model runs the convolution in PyTorch). */
+int qvggt_patchify(const void* images, void* out, int64_t S, int32_t H, int32_t W, int32_t patch, int32_t k_pad,
+                   const float* mean3, const float* std3, void* stream);
+
+/* out [S, P, C]: rows p < n_special of frame f copy specials[set][p] (set = 1
+ * for every frame whose global index f + frame_offset > 0 when two_sets != 0,
+ * else 0); rows p >= n_special copy src row
+ * f*src_rows_per_frame + src_row_offset + (p - n_special).  If pos != NULL,
+ * pos[p] (fp16 [P, C]) is added (one fp16 rounding).  Builds the DINOv2 token
+ * sequence (cls / registers / patches + position embedding) and the aggregator
+ * sequence (camera / registers / patch tokens).  No reference counterpart. */
+int qvggt_assemble_tokens(const void* src, int64_t src_rows_per_frame, int64_t src_row_offset, const void* specials,
+                          int32_t n_special, int32_t two_sets, const void* pos, void* out, int64_t S, int32_t P,
+                          int32_t C, int64_t frame_offset, void* stream);
+
 /* ------------------------------------------------------------- self-test */
 
 /* Runs one kernel whose bounded wait waits on an mbarrier nothing arrives on;

@@ -48,11 +48,15 @@ def gelu_erf(x: torch.Tensor) -> torch.Tensor:
     return r16(0.5 * xf * (1.0 + torch.erf(xf / math.sqrt(2.0))))
 
 
-def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, chunk: int = 4096) -> torch.Tensor:
-    """softmax(q k^T / sqrt(d)) v in fp32, q/k/v [..., L, d] fp16 -> fp16."""
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, chunk: int | None = None) -> torch.Tensor:
+    """softmax(q k^T / sqrt(d)) v in fp32, q/k/v [..., L, d] fp16 -> fp16.
+    Query rows are processed in chunks so the score block stays near 2e8 floats."""
     d = q.shape[-1]
     scale = 1.0 / math.sqrt(d)
     kf, vf = k.float(), v.float()
+    if chunk is None:
+        lead = max(1, q[..., 0, 0].numel())
+        chunk = max(64, int(2e8 // (lead * k.shape[-2])))
     outs = []
     for s in range(0, q.shape[-2], chunk):
         qf = q[..., s:s + chunk, :].float()

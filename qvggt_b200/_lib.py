@@ -38,6 +38,8 @@ SIGNATURES = {
     "qvggt_qkv_rope2d": [vp, vp, vp, i64, i32, i64, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp, f32, vp],
     "qvggt_attention": [vp, i64, vp, i64, i64, i64, vp, i64, i64, i64, i64, i32, vp],
     "qvggt_selftest_wait_timeout": [u64, u32p],
+    "qvggt_patchify": [vp, vp, i64, i32, i32, i32, i32, C.POINTER(f32), C.POINTER(f32), vp],
+    "qvggt_assemble_tokens": [vp, i64, i64, vp, i32, i32, vp, vp, i64, i32, i32, i64, vp],
 }
 _RESTYPES = {"qvggt_last_error": C.c_char_p, "qvggt_launch_count": C.c_uint64}
 

@@ -1,0 +1,303 @@
+"""VGGT aggregator forward on the sm_100a kernels.
+
+The aggregator (defined in the un-vendored ``vggt-hf`` model the reference
+loads at ``qvggt/inference/loader.py:27``) runs, after the DINOv2 patch embed,
+24 alternating frame / global block pairs over tokens [S, P, C]
+(P = 1 camera + 4 register + 37*37 patch tokens, C = 1024).  Each block is
+
+    x += ls1 * proj(attn(rope2d(q), rope2d(k), v)),  q, k, v = qkv(LN1(x))
+    x += ls2 * fc2(gelu(fc1(LN2(x))))
+
+with the frame block attending within each frame and the global block over
+all S*P tokens.  The reference quantises every qkv / proj / fc1 / fc2 of both
+block types to W4A16 (``loader.py:320-394``).
+
+Kernel sequence of one block (W4A16):
+
+    layernorm -> W4 GEMM(qkv, +bias) -> qkv_rope2d (split + 2-D RoPE)
+    -> flash attention -> W4 GEMM(proj, +bias, LayerScale residual, in place)
+    -> layernorm -> W4 GEMM(fc1, +bias, GELU) -> W4 GEMM(fc2, +bias, LayerScale residual)
+
+Multi-GPU: frames are sharded contiguously over ranks.  Frame blocks and all
+linears are rank-local; a global block writes its roped K / V straight into
+this rank's slice of a [S*P, 2C] buffer and all-gathers it over NCCL before the
+attention of the local queries against all keys.  No other communication.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import awq_inference_engine as eng
+
+F16 = torch.float16
+
+
+@dataclass
+class AggConfig:
+    dim: int = 1024
+    heads: int = 16
+    mlp_ratio: int = 4
+    depth: int = 24                  # frame/global block pairs
+    tokens_per_frame: int = 1374     # 1 camera + 4 register + 37*37 patches
+    patch_start: int = 5
+    grid_w: int = 37
+    eps: float = 1e-6
+    rope_base: float = 100.0
+    qk_norm: bool = False
+    group_size: int = 128
+    layer_scale: float = 0.01
+
+
+class Linear:
+    """A linear in one of three forms, holding device buffers:
+    ``w4`` (AWQ qweight / scales / scaled_zeros), ``f16`` (dense weight [N, K])."""
+
+    def __init__(self, kind: str, bias: torch.Tensor | None, group_size: int = 128, **bufs):
+        self.kind = kind
+        self.bias = bias
+        self.group_size = group_size
+        for k, v in bufs.items():
+            setattr(self, k, v)
+        if kind == "w4":
+            self.out_features = self.qweight.shape[0] * 4
+            self.in_features = self.qweight.shape[1]
+        else:
+            self.out_features, self.in_features = self.weight.shape
+
+    @classmethod
+    def from_oracle(cls, ql, device) -> "Linear":
+        """From an ``oracle.model.QLinear``-like object holding numpy buffers."""
+        t = lambda a: None if a is None else torch.as_tensor(np.ascontiguousarray(a)).to(device)
+        if ql.kind == "w4":
+            return cls("w4", t(ql.bias), ql.group_size, qweight=t(ql.qweight), scales=t(ql.scales),
+                       scaled_zeros=t(ql.scaled_zeros))
+        return cls("f16", t(ql.bias), weight=t(ql.weight))
+
+    def __call__(self, x, out=None, act=None, residual=None, gamma=None):
+        if self.kind == "w4":
+            return eng.w4a16_linear(x, self.qweight, self.scales, self.scaled_zeros, self.bias, self.group_size,
+                                    act=act, residual=residual, gamma=gamma, out=out)
+        return eng.f16_linear(x, self.weight, self.bias, act=act, residual=residual, gamma=gamma, out=out)
+
+
+@dataclass
+class Block:
+    norm1_w: torch.Tensor
+    norm1_b: torch.Tensor
+    qkv: Linear
+    proj: Linear
+    ls1: torch.Tensor
+    norm2_w: torch.Tensor
+    norm2_b: torch.Tensor
+    fc1: Linear
+    fc2: Linear
+    ls2: torch.Tensor
+    qk_norm: tuple | None = None
+
+    @classmethod
+    def from_oracle(cls, blk: dict, device) -> "Block":
+        t = lambda a: torch.as_tensor(np.ascontiguousarray(a)).to(device)
+        qn = None
+        if blk.get("qk_norm"):
+            qn = (t(blk["qn_w"]), t(blk["qn_b"]), t(blk["kn_w"]), t(blk["kn_b"]))
+        return cls(t(blk["norm1_w"]), t(blk["norm1_b"]), Linear.from_oracle(blk["qkv"], device),
+                   Linear.from_oracle(blk["proj"], device), t(blk["ls1"]), t(blk["norm2_w"]), t(blk["norm2_b"]),
+                   Linear.from_oracle(blk["fc1"], device), Linear.from_oracle(blk["fc2"], device), t(blk["ls2"]), qn)
+
+
+def rope_tables(cfg: AggConfig, device):
+    """cos / sin [max_pos, head_dim/2] fp16, computed as the model does (fp32
+    angles cast to fp16, then cos / sin rounded to fp16)."""
+    hd = cfg.dim // cfg.heads
+    f = hd // 2
+    max_pos = (cfg.tokens_per_frame - cfg.patch_start + cfg.grid_w - 1) // cfg.grid_w + 2
+    inv = 1.0 / (cfg.rope_base ** (torch.arange(0, f, 2, dtype=torch.float32) / f))
+    ang = torch.einsum("i,j->ij", torch.arange(max_pos, dtype=torch.float32), inv).to(F16)
+    ang = torch.cat([ang, ang], dim=-1).float()
+    return ang.cos().to(F16).to(device).contiguous(), ang.sin().to(F16).to(device).contiguous()
+
+
+class Workspace:
+    """Activation buffers for T local tokens (allocated once, reused by every block)."""
+
+    def __init__(self, T_local: int, T_global: int, cfg: AggConfig, device):
+        C = cfg.dim
+        self.h = torch.empty(T_local, C, dtype=F16, device=device)
+        self.qkv = torch.empty(T_local, 3 * C, dtype=F16, device=device)
+        self.q = torch.empty(T_local, C, dtype=F16, device=device)
+        self.kv_local = torch.empty(T_local, 2 * C, dtype=F16, device=device)
+        self.kv_global = torch.empty(T_global, 2 * C, dtype=F16, device=device)
+        self.attn = torch.empty(T_local, C, dtype=F16, device=device)
+        self.mlp = torch.empty(T_local, cfg.mlp_ratio * C, dtype=F16, device=device)
+
+
+class AggregatorRunner:
+    """Runs the aggregator block stack for this rank's frames.
+
+    ``frames_local`` frames of ``cfg.tokens_per_frame`` tokens live on this
+    rank; ``group`` (a torch.distributed process group, or None for one GPU)
+    provides the K/V all-gather of the global blocks.
+    """
+
+    def __init__(self, cfg: AggConfig, frame_blocks: list[Block], global_blocks: list[Block], frames_local: int,
+                 device, group=None, world: int = 1, rank: int = 0):
+        self.cfg = cfg
+        self.frame_blocks = frame_blocks
+        self.global_blocks = global_blocks
+        self.S_local = frames_local
+        self.world = world
+        self.rank = rank
+        self.group = group
+        self.device = torch.device(device)
+        P = cfg.tokens_per_frame
+        self.T = frames_local * P
+        self.ws = Workspace(self.T, self.T * world, cfg, self.device)
+        self.cos, self.sin = rope_tables(cfg, self.device)
+        # When a list: (start event, end event, algorithmic FLOP) of every
+        # global-attention launch is appended (CUDA events on the current stream).
+        self.kernel_timer = None
+
+    # ------------------------------------------------------------------ block
+    def block(self, x: torch.Tensor, blk: Block, kind: str, rope: bool = True) -> None:
+        """One block over x [T_local, C] in place.  ``rope=False`` (the DINOv2
+        patch-embed blocks) attends within each frame straight out of the qkv
+        buffer, without RoPE."""
+        cfg, ws = self.cfg, self.ws
+        P = cfg.tokens_per_frame
+        C = cfg.dim
+        eng.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, out=ws.h)
+        blk.qkv(ws.h, out=ws.qkv)
+        if not rope:
+            eng.attention(ws.qkv[:, :C], ws.qkv, cfg.heads, self.S_local, P, P, out=ws.attn, k_col0=C, v_col0=2 * C)
+            blk.proj(ws.attn, residual=x, gamma=blk.ls1)
+            eng.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, out=ws.h)
+            blk.fc1(ws.h, out=ws.mlp, act="gelu")
+            blk.fc2(ws.mlp, residual=x, gamma=blk.ls2)
+            return
+        glob = kind == "global"
+        if glob and self.world > 1:
+            kv_dst = ws.kv_global[self.rank * self.T:(self.rank + 1) * self.T]
+        else:
+            kv_dst = ws.kv_local
+        eng.qkv_rope2d(ws.qkv, cfg.heads, self.cos, self.sin, P, cfg.patch_start, cfg.grid_w, 0,
+                       q_out=ws.q, kv_out=kv_dst, qk_norm=blk.qk_norm, eps=cfg.eps)
+        if glob:
+            if self.world > 1:
+                torch.distributed.all_gather_into_tensor(ws.kv_global, kv_dst, group=self.group)
+                kv, Lkv = ws.kv_global, self.T * self.world
+            else:
+                kv, Lkv = ws.kv_local, self.T
+            if self.kernel_timer is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            eng.attention(ws.q, kv, cfg.heads, 1, self.T, Lkv, out=ws.attn)
+            if self.kernel_timer is not None:
+                ev1.record()
+                self.kernel_timer.append((ev0, ev1, 4.0 * self.T * Lkv * cfg.dim))
+        else:
+            eng.attention(ws.q, ws.kv_local, cfg.heads, self.S_local, P, P, out=ws.attn)
+        blk.proj(ws.attn, residual=x, gamma=blk.ls1)
+        eng.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, out=ws.h)
+        blk.fc1(ws.h, out=ws.mlp, act="gelu")
+        blk.fc2(ws.mlp, residual=x, gamma=blk.ls2)
+
+    def forward(self, tokens: torch.Tensor, keep: tuple[int, ...] = ()) -> dict:
+        """tokens [S_local, P, C] fp16 (modified in place).  Runs every pair;
+        returns {layer: (frame_out, global_out)} copies for the pair indices in
+        ``keep`` plus the final pair under key -1."""
+        x = tokens.view(self.T, self.cfg.dim)
+        outs = {}
+        n = len(self.frame_blocks)
+        for i in range(n):
+            self.block(x, self.frame_blocks[i], "frame")
+            fr = x.clone() if (i in keep or i == n - 1) else None
+            self.block(x, self.global_blocks[i], "global")
+            if fr is not None:
+                outs[-1 if i == n - 1 else i] = (fr, x.clone())
+        return outs
+
+
+
+@dataclass
+class PatchEmbed:
+    """DINOv2 ViT-L/14 with 4 registers (the aggregator's fp16, unquantised
+    front; excluded from quantisation at ``loader.py:346``)."""
+    patch_w: torch.Tensor      # [C, k_pad] fp16, column c*p*p + ky*p + kx, zero padded
+    patch_b: torch.Tensor      # [C]
+    specials: torch.Tensor     # [1, 5, C]: cls then 4 register tokens
+    pos: torch.Tensor          # [P, C]: pos[0] for cls, 0 for registers, pos[1+i] for patch i
+    blocks: list               # Block (kind f16), no RoPE
+    norm_w: torch.Tensor
+    norm_b: torch.Tensor
+    patch: int = 14
+    k_pad: int = 640
+
+
+class VGGTAggregator:
+    """Images [S_local, 3, H, W] -> aggregator outputs, on this rank's frames.
+
+    patchify -> patch GEMM -> [cls | registers | patches] + pos -> DINOv2 blocks
+    -> LayerNorm -> [camera | registers | patch tokens] (first frame of the
+    sequence uses its own camera / register tokens) -> 24 frame/global pairs.
+    """
+
+    def __init__(self, cfg: AggConfig, pe: PatchEmbed, agg_specials: torch.Tensor, frame_blocks, global_blocks,
+                 frames_local: int, device, group=None, world: int = 1, rank: int = 0, img_hw=(518, 518)):
+        self.cfg = cfg
+        self.pe = pe
+        self.agg_specials = agg_specials            # [2, 5, C]: camera + 4 registers, frame 0 / others
+        self.runner = AggregatorRunner(cfg, frame_blocks, global_blocks, frames_local, device, group, world, rank)
+        self.S_local = frames_local
+        self.rank = rank
+        self.img_hw = img_hw
+        H, W = img_hw
+        self.n_patch = (H // pe.patch) * (W // pe.patch)
+        assert self.n_patch + cfg.patch_start == cfg.tokens_per_frame
+        dev = torch.device(device)
+        C = cfg.dim
+        self.patches = torch.empty(frames_local * self.n_patch, pe.k_pad, dtype=F16, device=dev)
+        self.pe_out = torch.empty(frames_local * self.n_patch, C, dtype=F16, device=dev)
+        self.x_pe = torch.empty(frames_local, cfg.tokens_per_frame, C, dtype=F16, device=dev)
+        self.tokens = torch.empty(frames_local, cfg.tokens_per_frame, C, dtype=F16, device=dev)
+
+    def forward(self, images: torch.Tensor, keep: tuple[int, ...] = ()) -> dict:
+        cfg, pe = self.cfg, self.pe
+        P, C = cfg.tokens_per_frame, cfg.dim
+        eng.patchify(images, pe.patch, pe.k_pad, out=self.patches)
+        eng.f16_linear(self.patches, pe.patch_w, pe.patch_b, out=self.pe_out)
+        eng.assemble_tokens(self.pe_out, self.n_patch, 0, pe.specials, cfg.patch_start, False, pe.pos, self.x_pe,
+                            self.S_local, P)
+        x = self.x_pe.view(-1, C)
+        for blk in pe.blocks:
+            self.runner.block(x, blk, "frame", rope=False)
+        h = self.runner.ws.h
+        eng.layernorm(x, pe.norm_w, pe.norm_b, cfg.eps, out=h)
+        eng.assemble_tokens(h, P, cfg.patch_start, self.agg_specials, cfg.patch_start, True, None, self.tokens,
+                            self.S_local, P, frame_offset=self.rank * self.S_local)
+        return self.runner.forward(self.tokens, keep)
+
+    def infer(self, images_host: torch.Tensor, out_host: torch.Tensor | None = None):
+        """Public end-to-end call: host images [S_local, 3, H, W] fp16 (pinned
+        for asynchronous copies) -> host tensor [S_local, P, 2C] holding the
+        last pair's (frame output | global output), the tokens VGGT's heads read.
+        Copies in and out run on the current stream; returns after the copy out."""
+        dev = self.tokens.device
+        C, P = self.cfg.dim, self.cfg.tokens_per_frame
+        if not hasattr(self, "_img_dev") or self._img_dev.shape != images_host.shape:
+            self._img_dev = torch.empty(images_host.shape, dtype=F16, device=dev)
+            self._cat = torch.empty(self.S_local, P, 2 * C, dtype=F16, device=dev)
+        self._img_dev.copy_(images_host, non_blocking=True)
+        outs = self.forward(self._img_dev)
+        fr, gl = outs[-1]
+        self._cat[..., :C].copy_(fr.view(self.S_local, P, C))
+        self._cat[..., C:].copy_(gl.view(self.S_local, P, C))
+        if out_host is None:
+            out_host = torch.empty(self._cat.shape, dtype=F16, pin_memory=True)
+        out_host.copy_(self._cat, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return out_host

@@ -315,6 +315,41 @@ def qkv_rope2d(qkv, heads: int, cos_tab, sin_tab, tokens_per_frame: int = 1374, 
     return q_out, kv_out
 
 
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+
+
+def patchify(images, patch: int = 14, k_pad: int = 640, out=None, mean=IMAGENET_MEAN, std=IMAGENET_STD):
+    """images fp16 [S, 3, H, W] -> normalised patches [S*(H/p)*(W/p), k_pad]."""
+    name = "patchify"
+    dev = _check_cuda(name, images)
+    _contig(name, images)
+    S, _, H, W = images.shape
+    rows = S * (H // patch) * (W // patch)
+    if out is None:
+        out = torch.empty(rows, k_pad, dtype=F16_, device=dev)
+    m = (C.c_float * 3)(*mean)
+    s = (C.c_float * 3)(*std)
+    with _Dev(dev):
+        _lib.call("qvggt_patchify", _ptr(images), _ptr(out), S, H, W, patch, k_pad, m, s, _stream(images))
+    return out
+
+
+def assemble_tokens(src, src_rows_per_frame: int, src_row_offset: int, specials, n_special: int, two_sets: bool,
+                    pos, out, S: int, P: int, frame_offset: int = 0):
+    """out [S, P, C] = per-frame [specials | src rows] (+ pos)."""
+    name = "assemble_tokens"
+    dev = _check_cuda(name, src, specials, pos, out)
+    Cd = out.shape[-1]
+    with _Dev(dev):
+        _lib.call("qvggt_assemble_tokens", _ptr(src), src_rows_per_frame, src_row_offset, _ptr(specials), n_special,
+                  1 if two_sets else 0, _ptr(pos), _ptr(out), S, P, Cd, frame_offset, _stream(out))
+    return out
+
+
+F16_ = torch.float16
+
+
 def attention(q, kv, heads: int, batches: int, Lq: int, Lkv: int, out=None, k_col0: int | None = None,
               v_col0: int | None = None):
     """Flash attention (head_dim 64) over token-major q [batches*Lq, heads*64]
