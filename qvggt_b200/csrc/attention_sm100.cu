@@ -2,17 +2,19 @@
 //
 // One CTA per (batch, head, block of 256 query rows) = two 128-row Q tiles
 // that share every K/V tile loaded into shared memory.  Per KV tile j of 128
-// keys:
+// keys and Q tile i:
 //   S_i = Q_i K_j^T        (tcgen05.mma, fp16 x fp16 -> fp32 in TMEM)
-//   P_i = exp2(S_i*c - m)  (softmax warpgroup i: one thread per query row,
-//                           tcgen05.ld of its S row, fp16 P written back to TMEM)
+//   P_i = exp2(S_i*c - m)  (softmax warpgroup i: one thread per query row reads
+//                           its whole S row from TMEM once, then computes)
 //   O_i += P_i V_j         (tcgen05.mma with A = P read from TMEM, B = V from
 //                           shared memory in the MN-major 128-byte-swizzled layout)
+// Schedule: a softmax warpgroup releases S_i (s_free) as soon as its TMEM read
+// of the row completes, so the tensor core computes S_i(j+1) while the
+// warpgroup is still exponentiating tile j; P_i is written only after
+// PV_i(j-1) has finished reading the previous P_i (o_done).
 // The running maximum m is only raised when a row's new maximum exceeds it by
 // more than 2^8 (then O_i and the row sum are rescaled in place); P <= 256 fits
-// fp16 and the final O / l is exact either way.  While warpgroup 0 turns S_0
-// into P_0 the tensor core computes S_1 (and vice versa), so MMA and softmax
-// overlap.
+// fp16 and the final O / l is exact either way.
 //
 // TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 //               O0 [384,448) O1 [448,512).
@@ -36,8 +38,8 @@ struct AttnSmem {
   static constexpr int K = Q1 + TILE_BYTES;
   static constexpr int V = K + KV_STAGES * TILE_BYTES;
   static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
-  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_done[2], drain
-  static constexpr int NUM_BARS = 1 + 3 * KV_STAGES + 6 + 1;
+  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], o_done[2], drain
+  static constexpr int NUM_BARS = 1 + 3 * KV_STAGES + 8 + 1;
   static constexpr int MISC = BAR + NUM_BARS * 8;
   static constexpr int TOTAL = MISC + 16 + 1024;
 };
@@ -57,6 +59,48 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Loads the thread's 128 S values (4 x 32 columns) with one wait.
+__device__ __forceinline__ void load_s_row(uint32_t tS, uint32_t (&s)[128]) {
+  tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+  tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+  tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+  tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+  tmem_ld_wait();
+}
+
+template <bool PARTIAL>
+__device__ __forceinline__ float row_max(const uint32_t (&s)[128], int valid) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < 128; e += 4) {
+    if (!PARTIAL || e + 0 < valid) m0 = fmaxf(m0, __uint_as_float(s[e + 0]));
+    if (!PARTIAL || e + 1 < valid) m1 = fmaxf(m1, __uint_as_float(s[e + 1]));
+    if (!PARTIAL || e + 2 < valid) m2 = fmaxf(m2, __uint_as_float(s[e + 2]));
+    if (!PARTIAL || e + 3 < valid) m3 = fmaxf(m3, __uint_as_float(s[e + 3]));
+  }
+  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
+
+// p = exp2(s*c - m) (0 beyond `valid`), accumulated into l, packed as fp16
+// pairs into s[0..63] (in place: pair e is read before slot e is written).
+template <bool PARTIAL>
+__device__ __forceinline__ float exp_pack(uint32_t (&s)[128], float c, float neg_m, int valid) {
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int e = 0; e < 64; ++e) {
+    float p0 = ex2(fmaf(__uint_as_float(s[2 * e]), c, neg_m));
+    float p1 = ex2(fmaf(__uint_as_float(s[2 * e + 1]), c, neg_m));
+    if (PARTIAL) {
+      if (2 * e >= valid) p0 = 0.f;
+      if (2 * e + 1 >= valid) p1 = 0.f;
+    }
+    l0 += p0;
+    l1 += p1;
+    s[e] = pack_half2(p0, p1);
+  }
+  return l0 + l1;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
@@ -67,9 +111,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + KV_STAGES;
   uint64_t* kv_empty = v_full + KV_STAGES;
-  uint64_t* s_full = kv_empty + KV_STAGES;  // [2]
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_done = p_full + 2;            // [2]
+  uint64_t* s_full = kv_empty + KV_STAGES;  // [2] MMA -> softmax: S_i ready
+  uint64_t* s_free = s_full + 2;            // [2] softmax -> MMA: S_i read
+  uint64_t* p_full = s_free + 2;            // [2] softmax -> MMA: P_i written
+  uint64_t* o_done = p_full + 2;            // [2] MMA -> softmax: PV_i complete
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AttnSmem::MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + AttnSmem::MISC + 4);
@@ -91,6 +136,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
     }
@@ -112,7 +158,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  // Registers: launched at 168 per thread (384 x 168 = 64512); warpgroup 0
+  // (producer, MMA, two idle warps) gives back to 56, the two softmax
+  // warpgroups take 216 each: 128*56 + 256*216 = 62464 <= 64512.
+  if (warp < 4) {
+    regs_dec<56>();
+    if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
@@ -155,54 +206,47 @@ __global__ void __launch_bounds__(THREADS, 1)
                      (jj > 0 || k > 0) ? 1u : 0u);
         tc_commit(&o_done[i]);
       };
-      int j = 0;
-      for (; ok && j < nkv; ++j) {
+      // PV_0(jj), PV_1(jj), then release K/V stage of tile jj.
+      auto pv_pair = [&](int jj) -> bool {
+        for (int i = 0; i < 2; ++i) {
+          if (!mbar_wait(&p_full[i], jj & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) return false;
+          if (i == 0 && !mbar_wait(&v_full[jj % KV_STAGES], (jj / KV_STAGES) & 1, abort_flag, a.ctl,
+                                   ST_TIMEOUT_FULL))
+            return false;
+          tc_fence_after();
+          issue_pv(i, jj);
+        }
+        tc_commit(&kv_empty[jj % KV_STAGES]);
+        return true;
+      };
+      for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % KV_STAGES;
         if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
-        tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + AttnSmem::K + st * TILE_BYTES);
         for (int i = 0; i < 2; ++i) {
-          if (j > 0) {
-            if (!mbar_wait(&p_full[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
-            if (i == 0) {
-              const int sp = (j - 1) % KV_STAGES;
-              if (!mbar_wait(&v_full[sp], ((j - 1) / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
-                ok = false;
-                break;
-              }
-            }
-            tc_fence_after();
-            issue_pv(i, j - 1);
-            if (i == 1) tc_commit(&kv_empty[(j - 1) % KV_STAGES]);
+          if (j > 0 && !mbar_wait(&s_free[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_f16_ss(tmem + COL_S0 + i * 128, sdesc_sw128(q_addr[i] + k * 32), sdesc_sw128(k_addr + k * 32),
                        idesc_s, k > 0 ? 1u : 0u);
           tc_commit(&s_full[i]);
         }
+        if (ok && j > 0) ok = pv_pair(j - 1);
       }
-      if (ok && nkv > 0) {
-        const int jl = nkv - 1;
-        for (int i = 0; i < 2 && ok; ++i) {
-          if (!mbar_wait(&p_full[i], jl & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
-          if (i == 0 &&
-              !mbar_wait(&v_full[jl % KV_STAGES], (jl / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(i, jl);
-        }
-        if (ok) tc_commit(&kv_empty[jl % KV_STAGES]);
-      }
+      if (ok && nkv > 0) ok = pv_pair(nkv - 1);
       if (!ok) {
         tc_commit(drain);
         mbar_wait_drain(drain, 0, 200000000ull);
       }
     }
+    }
   } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ softmax WG i
+    regs_inc<216>();
     const int i = (warp - 4) / 4;
     const int quarter = warp & 3;             // TMEM lane quarter
     const int r = quarter * 32 + lane;        // row within the Q tile
@@ -216,31 +260,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait_warp(&s_full[i], j & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
       tc_fence_after();
+      uint32_t s[128];
+      load_s_row(tS, s);
+      // S_i is in registers: hand the TMEM columns back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[i]);
+
       const long long rem = a.Lkv - (long long)j * 128;
       const int valid = rem >= 128 ? 128 : (int)rem;
-      // pass 1: row maximum of the raw scores
-      float mx = -INFINITY;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(tS + cc * 32, v);
-        tmem_ld_wait();
-        if (valid == 128) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (cc * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(v[e]));
-        }
-      }
+      const float mx = (valid == 128) ? row_max<false>(s, valid) : row_max<true>(s, valid);
       const float m_new = fmaxf(m_used, mx * c);
       const bool need = m_new > m_used + 8.0f;
+      bool o_ready = (j == 0);   // PV_i(j-1) complete (nothing to wait for at j = 0)
       if (__any_sync(0xffffffffu, need)) {
         const float m_target = need ? m_new : m_used;
         const float alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_target);
         if (j > 0) {
           if (!mbar_wait_warp(&o_done[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+          o_ready = true;
           tc_fence_after();
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
@@ -251,32 +289,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
             tmem_st16(tO + cc * 16, v);
           }
-          tmem_st_wait();
         }
         l *= alpha;
         m_used = m_target;
       }
-      // pass 2: P = exp2(S*c - m), row sum, fp16 P into TMEM
-      const float neg_m = -m_used;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(tS + cc * 32, v);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float p0 = ex2(fmaf(__uint_as_float(v[2 * e]), c, neg_m));
-          float p1 = ex2(fmaf(__uint_as_float(v[2 * e + 1]), c, neg_m));
-          if (valid < 128) {
-            if (cc * 32 + 2 * e >= valid) p0 = 0.f;
-            if (cc * 32 + 2 * e + 1 >= valid) p1 = 0.f;
-          }
-          l += p0 + p1;
-          pk[e] = pack_half2(p0, p1);
-        }
-        tmem_st16(tP + cc * 16, pk);
+      l += (valid == 128) ? exp_pack<false>(s, c, -m_used, valid) : exp_pack<true>(s, c, -m_used, valid);
+      // P_i may be overwritten only once PV_i(j-1) has read it
+      if (!o_ready) {
+        if (!mbar_wait_warp(&o_done[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+        tc_fence_after();
       }
+      tmem_st16(tP + 0, *reinterpret_cast<const uint32_t(*)[16]>(&s[0]));
+      tmem_st16(tP + 16, *reinterpret_cast<const uint32_t(*)[16]>(&s[16]));
+      tmem_st16(tP + 32, *reinterpret_cast<const uint32_t(*)[16]>(&s[32]));
+      tmem_st16(tP + 48, *reinterpret_cast<const uint32_t(*)[16]>(&s[48]));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();

@@ -1,0 +1,163 @@
+"""Golden outputs of the reference's own CUDA kernels, run on a B200.
+
+    python oracle/build_ref.py            # in the container with the reference checkout
+    python tests/golden/make_ref_cuda_golden.py --out ref_cuda_golden.npz [--time]
+
+Runs the reference kernels (built from their own sources into oracle/_ref/ by
+oracle/build_ref.py) on inputs generated from fixed seeds (regenerated
+identically by the tests, see ``cases()``), and stores only the outputs.
+``--time`` also prints CUDA-event timings of the reference kernels at the
+benchmark shapes.
+
+Not run: the reference GEMM with M <= 32.  That path (gemm_w4a16_T1 with
+SPLITK = 2) waits on split-K semaphores allocated with torch::empty, i.e.
+uninitialised (gemm_cuda.cu:28, semaphore.h:35-43), and can spin forever.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+
+def cases():
+    """Seeded inputs shared by this generator and the tests (numpy, CPU)."""
+    from oracle import awq
+    c = {}
+    for name, (M, N, K, seed) in {"gemm_a": (300, 512, 1024, 10), "gemm_b": (256, 256, 4096, 11)}.items():
+        lin = awq.make_quantized_linear(N, K, 128, seed=seed, bias=False)
+        x = np.random.default_rng(seed + 100).standard_normal((M, K)).astype(np.float16)
+        c[name] = dict(x=x, qweight=lin["qweight"], scales=lin["scales"], scaled_zeros=lin["scaled_zeros"])
+    rng = np.random.default_rng(20)
+    c["w8a8"] = dict(a=rng.integers(-127, 128, (200, 512)).astype(np.int8),
+                     w=rng.integers(-127, 128, (256, 512)).astype(np.int8),
+                     ws=(rng.random(256) * 1e-3 + 1e-4).astype(np.float16),
+                     as_=(rng.random(200) * 1e-2 + 1e-3).astype(np.float16),
+                     bias=(rng.standard_normal(256) * 0.1).astype(np.float16))
+    rng = np.random.default_rng(21)
+    c["quant"] = dict(x=(rng.standard_normal((200, 1024)) * 3).astype(np.float16))
+    rng = np.random.default_rng(22)
+    c["ln"] = dict(x=(rng.standard_normal((200, 1024)) * 2 + 0.5).astype(np.float16),
+                   w=(1 + 0.1 * rng.standard_normal(1024)).astype(np.float16),
+                   b=(0.1 * rng.standard_normal(1024)).astype(np.float16))
+    rng = np.random.default_rng(23)
+    c["gelu"] = dict(x=(rng.standard_normal((128, 1024)) * 2).astype(np.float16))
+    rng = np.random.default_rng(24)
+    c["rope"] = dict(x=rng.standard_normal((37, 2, 16, 64)).astype(np.float16),
+                     freqs=(rng.random((2, 37, 32)) * 10).astype(np.float32))
+    return c
+
+
+def generate(ref, dev="cuda"):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    out = {}
+    c = cases()
+    for name in ("gemm_a", "gemm_b"):
+        d = c[name]
+        y = ref.gemm_forward_cuda_new(t(d["x"]), t(d["qweight"]), t(d["scales"]), t(d["scaled_zeros"]))
+        out[f"{name}_y"] = y.cpu().numpy()
+    d = c["gemm_a"]
+    for m in (1, 7):
+        K, N = d["x"].shape[1], d["qweight"].shape[0] * 4
+        y = ref.gemv_forward_cuda_new(t(d["x"][:m]), t(d["qweight"]), t(d["scales"]), t(d["scaled_zeros"]), m, N, K,
+                                      128)
+        out[f"gemv_m{m}_y"] = y.cpu().numpy()
+    d = c["w8a8"]
+    o = torch.empty(200, 256, dtype=torch.float16, device=dev)
+    ref.w8a8_gemm_forward_cuda(t(d["a"]), t(d["w"]), t(d["ws"]), t(d["as_"]), o)
+    out["w8a8_y"] = o.cpu().numpy()
+    o2 = torch.empty(200, 256, dtype=torch.float16, device=dev)
+    ref.w8a8_gemm_fuse_bias_forward_cuda(t(d["a"]), t(d["w"]), t(d["ws"]), t(d["as_"]), o2, t(d["bias"]))
+    out["w8a8_bias_y"] = o2.cpu().numpy()
+    x = t(c["quant"]["x"])
+    q = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    s = torch.empty(x.shape[0], dtype=torch.float16, device=dev)
+    ref.invoke_quant(q, x, s)
+    out["quant_q"], out["quant_s"] = q.cpu().numpy(), s.cpu().numpy()
+    d = c["ln"]
+    x = t(d["x"])
+    q = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    s = torch.empty(x.shape[0], dtype=torch.float16, device=dev)
+    ref.rms_norm_general(q, x, t(d["w"]), t(d["b"]), s, 1e-6, True)
+    out["ln_q"], out["ln_s"] = q.cpu().numpy(), s.cpu().numpy()
+    q2 = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    s2 = torch.tensor([20.0], dtype=torch.float16, device=dev)
+    ref.rms_norm_general(q2, x, t(d["w"]), t(d["b"]), s2, 1e-6, False)
+    out["ln_tensor_q"] = q2.cpu().numpy()
+    x = t(c["gelu"]["x"])
+    q = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    s = torch.empty(x.shape[0], dtype=torch.float16, device=dev)
+    tmp = torch.empty(x.shape, dtype=torch.float16, device=dev)
+    ref.gelu_and_quant(q, x, s, tmp)
+    out["gelu_q"], out["gelu_s"], out["gelu_tmp"] = q.cpu().numpy(), s.cpu().numpy(), tmp.cpu().numpy()
+    d = c["rope"]
+    for tr in (False, True):
+        y = ref.fused_rope_with_pos_forward_func(t(d["x"]), t(d["freqs"]), tr)
+        out[f"rope_y_{int(tr)}"] = y.contiguous().cpu().numpy()
+    torch.cuda.synchronize()
+    return out
+
+
+def time_reference(ref, dev="cuda"):
+    """CUDA-event timings of the reference kernels at the benchmark shapes."""
+    from oracle import awq
+
+    def timeit(fn, iters=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / iters / 1e3
+
+    res = {}
+    for (M, N, K) in [(1374, 4096, 1024), (43968, 3072, 1024), (43968, 1024, 1024), (43968, 4096, 1024),
+                      (43968, 1024, 4096)]:
+        lin = awq.make_quantized_linear(N, K, 128, seed=1, bias=False)
+        qw, s, z = (torch.from_numpy(lin[k]).to(dev) for k in ("qweight", "scales", "scaled_zeros"))
+        x = torch.randn(M, K, dtype=torch.float16, device=dev)
+        sec = timeit(lambda: ref.gemm_forward_cuda_new(x, qw, s, z))
+        res[f"gemm_w4a16 M={M} N={N} K={K}"] = (sec * 1e6, 2 * M * N * K / sec / 1e12)
+    lin = awq.make_quantized_linear(4096, 1024, 128, seed=1, bias=False)
+    qw, s, z = (torch.from_numpy(lin[k]).to(dev) for k in ("qweight", "scales", "scaled_zeros"))
+    x1 = torch.randn(1, 1024, dtype=torch.float16, device=dev)
+    sec = timeit(lambda: ref.gemv_forward_cuda_new(x1, qw, s, z, 1, 4096, 1024, 128), iters=200)
+    res["gemv_w4a16 m=1 N=4096 K=1024"] = (sec * 1e6, 2 * 4096 * 1024 / sec / 1e12)
+    M, N, K = 87936, 4096, 1024
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev)
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+    ws = torch.rand(N, device=dev).half()
+    as_ = torch.rand(M, device=dev).half()
+    o = torch.empty(M, N, dtype=torch.float16, device=dev)
+    sec = timeit(lambda: ref.w8a8_gemm_forward_cuda(a, w, ws, as_, o))
+    res[f"w8a8_gemm M={M} N={N} K={K}"] = (sec * 1e6, 2 * M * N * K / sec / 1e12)
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "ref_cuda_golden.npz"))
+    ap.add_argument("--time", action="store_true")
+    a = ap.parse_args()
+    from oracle import build_ref
+    ref = build_ref.load()
+    out = generate(ref)
+    np.savez_compressed(a.out, **out)
+    print("wrote", a.out, {k: v.shape for k, v in out.items()})
+    if a.time:
+        for k, (us, tf) in time_reference(ref).items():
+            print(f"REF {k}: {us:.1f} us  {tf:.1f} TFLOP/s")
+
+
+if __name__ == "__main__":
+    main()
