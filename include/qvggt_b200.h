@@ -74,6 +74,22 @@ int qvggt_w4a16_linear_ex(const void* in_feats, int64_t lda, const void* qweight
                           int64_t K, int64_t gpad, int32_t group_size, int32_t act, const void* resid,
                           int64_t ldr, const void* gamma, void* stream);
 
+/* The qkv projection of a VGGT block with the q/k/v split, the optional per-head
+ * LayerNorm (qk_norm != 0; qn_w/qn_b/kn_w/kn_b fp16 [64]) and the 2-D RoPE
+ * fused into the W4A16 GEMM epilogue: y = half(half(in . deq(W)^T) + bias)
+ * over N = 3*dim columns [q | k | v]; q -> q_out [M, dim] and [k | v] ->
+ * kv_out [M, 2*dim], with q and k rotated exactly as qvggt_qkv_rope2d does
+ * (same position rule and fp16 rounding points).  weight_kind 0 = W4A16
+ * (qweight/scales/scaled_zeros/gpad/group_size), 1 = dense fp16 [N, K] in
+ * `qweight` (scales ignored).  New entry point (the reference model runs the
+ * split and RoPE in PyTorch after WQLinear.forward). */
+int qvggt_qkv_rope_linear(const void* in_feats, int32_t weight_kind, const void* qweight, const void* scales,
+                          const void* scaled_zeros, int64_t gpad, int32_t group_size, const void* bias, void* q_out,
+                          void* kv_out, int64_t M, int64_t K, int32_t dim, int64_t token_offset,
+                          int32_t tokens_per_frame, int32_t patch_start, int32_t grid_w, const void* cos_tab,
+                          const void* sin_tab, int32_t max_pos, int32_t qk_norm, const void* qn_w, const void* qn_b,
+                          const void* kn_w, const void* kn_b, float eps, void* stream);
+
 /* Dense fp16 linear with the same fused epilogues (weight fp16 [N, K]); used
  * for the unquantised DINOv2 patch-embed blocks.  No reference counterpart
  * (the reference runs these layers in PyTorch). */

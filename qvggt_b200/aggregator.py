@@ -14,7 +14,7 @@ block types to W4A16 (``loader.py:320-394``).
 
 Kernel sequence of one block (W4A16):
 
-    layernorm -> W4 GEMM(qkv, +bias) -> qkv_rope2d (split + 2-D RoPE)
+    layernorm -> W4 GEMM(qkv, +bias, q/k/v split + 2-D RoPE in the epilogue)
     -> flash attention -> W4 GEMM(proj, +bias, LayerScale residual, in place)
     -> layernorm -> W4 GEMM(fc1, +bias, GELU) -> W4 GEMM(fc2, +bias, LayerScale residual)
 
@@ -32,6 +32,7 @@ import numpy as np
 import torch
 
 from . import awq_inference_engine as eng
+from .dist import gather_kv, kv_slice
 
 F16 = torch.float16
 
@@ -170,8 +171,8 @@ class AggregatorRunner:
         P = cfg.tokens_per_frame
         C = cfg.dim
         eng.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, out=ws.h)
-        blk.qkv(ws.h, out=ws.qkv)
         if not rope:
+            blk.qkv(ws.h, out=ws.qkv)
             eng.attention(ws.qkv[:, :C], ws.qkv, cfg.heads, self.S_local, P, P, out=ws.attn, k_col0=C, v_col0=2 * C)
             blk.proj(ws.attn, residual=x, gamma=blk.ls1)
             eng.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, out=ws.h)
@@ -180,15 +181,15 @@ class AggregatorRunner:
             return
         glob = kind == "global"
         if glob and self.world > 1:
-            kv_dst = ws.kv_global[self.rank * self.T:(self.rank + 1) * self.T]
+            kv_dst = kv_slice(ws.kv_global, self.T, self.rank)
         else:
             kv_dst = ws.kv_local
-        eng.qkv_rope2d(ws.qkv, cfg.heads, self.cos, self.sin, P, cfg.patch_start, cfg.grid_w, 0,
-                       q_out=ws.q, kv_out=kv_dst, qk_norm=blk.qk_norm, eps=cfg.eps)
+        # qkv projection with the q/k/v split and 2-D RoPE in the GEMM epilogue
+        eng.qkv_rope_linear(ws.h, blk.qkv, cfg.heads, self.cos, self.sin, P, cfg.patch_start, cfg.grid_w, 0,
+                            q_out=ws.q, kv_out=kv_dst, qk_norm=blk.qk_norm, eps=cfg.eps)
         if glob:
             if self.world > 1:
-                torch.distributed.all_gather_into_tensor(ws.kv_global, kv_dst, group=self.group)
-                kv, Lkv = ws.kv_global, self.T * self.world
+                kv, Lkv = gather_kv(ws.kv_global, self.T, self.rank, self.group), self.T * self.world
             else:
                 kv, Lkv = ws.kv_local, self.T
             if self.kernel_timer is not None:

@@ -146,6 +146,35 @@ def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 
     return out
 
 
+def qkv_rope_linear(x, lin, heads: int, cos_tab, sin_tab, tokens_per_frame: int = 1374, patch_start: int = 5,
+                    grid_w: int = 37, token_offset: int = 0, q_out=None, kv_out=None, qk_norm=None,
+                    eps: float = 1e-6):
+    """qkv projection (W4A16 ``lin.kind == 'w4'`` or dense fp16) with the
+    split and VGGT 2-D RoPE fused into the GEMM epilogue.
+    Returns (q [M, C] roped, kv [M, 2C] = [k roped | v])."""
+    name = "qkv_rope_linear"
+    dev = _check_cuda(name, x, lin.bias, cos_tab, sin_tab)
+    _contig(name, x, cos_tab, sin_tab)
+    K = x.shape[-1]
+    M = x.numel() // K
+    Cd = heads * 64
+    if q_out is None:
+        q_out = torch.empty(M, Cd, dtype=torch.float16, device=dev)
+    if kv_out is None:
+        kv_out = torch.empty(M, 2 * Cd, dtype=torch.float16, device=dev)
+    qn = qk_norm if qk_norm is not None else (None, None, None, None)
+    if lin.kind == "w4":
+        wk, b, s, z, gpad, G = 0, lin.qweight, lin.scales, lin.scaled_zeros, lin.scales.shape[0], lin.group_size
+    else:
+        wk, b, s, z, gpad, G = 1, lin.weight, None, None, 0, 128
+    with _Dev(dev):
+        _lib.call("qvggt_qkv_rope_linear", _ptr(x), wk, _ptr(b), _ptr(s), _ptr(z), gpad, G, _ptr(lin.bias),
+                  _ptr(q_out), _ptr(kv_out), M, K, Cd, token_offset, tokens_per_frame, patch_start, grid_w,
+                  _ptr(cos_tab), _ptr(sin_tab), cos_tab.shape[0], 1 if qk_norm is not None else 0, _ptr(qn[0]),
+                  _ptr(qn[1]), _ptr(qn[2]), _ptr(qn[3]), float(eps), _stream(x))
+    return q_out, kv_out
+
+
 def f16_linear(x, weight, bias=None, act: str | None = None, residual=None, gamma=None, out=None):
     """Dense fp16 linear (weight [N, K]) with the same fused epilogues."""
     name = "f16_linear"

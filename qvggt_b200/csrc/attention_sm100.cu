@@ -20,6 +20,8 @@
 //               O0 [384,448) O1 [448,512).
 // Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 4..7 softmax WG 0,
 // 8..11 softmax WG 1.  All waits are bounded (common.cuh).
+#include <cstdlib>
+
 #include "host.hpp"
 
 namespace qv {
@@ -71,36 +73,88 @@ __device__ __forceinline__ void load_s_row(uint32_t tS, uint32_t (&s)[128]) {
 template <bool PARTIAL>
 __device__ __forceinline__ float row_max(const uint32_t (&s)[128], int valid) {
   float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+  if (!PARTIAL) {
+    // three-input max: 64 instructions for 128 scores, four independent chains
 #pragma unroll
-  for (int e = 0; e < 128; e += 4) {
-    if (!PARTIAL || e + 0 < valid) m0 = fmaxf(m0, __uint_as_float(s[e + 0]));
-    if (!PARTIAL || e + 1 < valid) m1 = fmaxf(m1, __uint_as_float(s[e + 1]));
-    if (!PARTIAL || e + 2 < valid) m2 = fmaxf(m2, __uint_as_float(s[e + 2]));
-    if (!PARTIAL || e + 3 < valid) m3 = fmaxf(m3, __uint_as_float(s[e + 3]));
+    for (int e = 0; e < 128; e += 8) {
+      m0 = max3f(m0, __uint_as_float(s[e + 0]), __uint_as_float(s[e + 1]));
+      m1 = max3f(m1, __uint_as_float(s[e + 2]), __uint_as_float(s[e + 3]));
+      m2 = max3f(m2, __uint_as_float(s[e + 4]), __uint_as_float(s[e + 5]));
+      m3 = max3f(m3, __uint_as_float(s[e + 6]), __uint_as_float(s[e + 7]));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 128; e += 4) {
+      if (e + 0 < valid) m0 = fmaxf(m0, __uint_as_float(s[e + 0]));
+      if (e + 1 < valid) m1 = fmaxf(m1, __uint_as_float(s[e + 1]));
+      if (e + 2 < valid) m2 = fmaxf(m2, __uint_as_float(s[e + 2]));
+      if (e + 3 < valid) m3 = fmaxf(m3, __uint_as_float(s[e + 3]));
+    }
   }
   return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
 }
 
+// 2^x for a pair of arguments on the FMA pipe (Cody-Waite range reduction:
+// x = n + f, n = round(x), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial
+// fitted to minimise the relative error on [-1/2, 1/2] (max 7.5e-5, well under
+// the fp16 rounding P gets afterwards); 2^n added into the exponent field).
+// Arguments are clamped at -125 so 2^n stays a normal float; those values
+// round to 0 in fp16 anyway.
+__device__ __forceinline__ void exp2_poly_pair(uint64_t x2, float& p0, float& p1) {
+  const uint64_t MAGIC = f2_pack(12582912.0f, 12582912.0f);        // 1.5 * 2^23: rounds to an integer
+  const uint64_t NEG_MAGIC = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t NEG_ONE = f2_pack(-1.0f, -1.0f);
+  const uint64_t C0 = f2_pack(0.99992806f, 0.99992806f), C1 = f2_pack(0.69326097f, 0.69326097f);
+  const uint64_t C2 = f2_pack(0.24261114f, 0.24261114f), C3 = f2_pack(0.05517166f, 0.05517166f);
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = f2_add(xc, MAGIC);          // low mantissa bits hold n
+  const uint64_t nf = f2_add(t, NEG_MAGIC);      // n as a float
+  const uint64_t f = f2_fma(nf, NEG_ONE, xc);    // x - n
+  uint64_t p = f2_fma(C3, f, C2);
+  p = f2_fma(p, f, C1);
+  p = f2_fma(p, f, C0);
+  float q0, q1, t0, t1;
+  f2_unpack(p, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 // p = exp2(s*c - m) (0 beyond `valid`), accumulated into l, packed as fp16
 // pairs into s[0..63] (in place: pair e is read before slot e is written).
-template <bool PARTIAL>
+// POLY of every 8 pairs use the FMA-pipe polynomial, the rest MUFU ex2, which
+// balances the two pipes (MUFU issues 16 results per SM per clock).
+template <bool PARTIAL, int POLY>
 __device__ __forceinline__ float exp_pack(uint32_t (&s)[128], float c, float neg_m, int valid) {
-  float l0 = 0.f, l1 = 0.f;
+  const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
+  uint64_t l2 = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int e = 0; e < 64; ++e) {
-    float p0 = ex2(fmaf(__uint_as_float(s[2 * e]), c, neg_m));
-    float p1 = ex2(fmaf(__uint_as_float(s[2 * e + 1]), c, neg_m));
+    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), c2, nm2);
+    float p0, p1;
+    if ((e & 7) < POLY) {
+      exp2_poly_pair(x2, p0, p1);
+    } else {
+      float x0, x1;
+      f2_unpack(x2, x0, x1);
+      p0 = ex2(x0);
+      p1 = ex2(x1);
+    }
     if (PARTIAL) {
       if (2 * e >= valid) p0 = 0.f;
       if (2 * e + 1 >= valid) p1 = 0.f;
     }
-    l0 += p0;
-    l1 += p1;
+    l2 = f2_add(l2, f2_pack(p0, p1));
     s[e] = pack_half2(p0, p1);
   }
+  float l0, l1;
+  f2_unpack(l2, l0, l1);
   return l0 + l1;
 }
 
+template <int POLY>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
@@ -293,7 +347,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         l *= alpha;
         m_used = m_target;
       }
-      l += (valid == 128) ? exp_pack<false>(s, c, -m_used, valid) : exp_pack<true>(s, c, -m_used, valid);
+      l += (valid == 128) ? exp_pack<false, POLY>(s, c, -m_used, valid) : exp_pack<true, POLY>(s, c, -m_used, valid);
       // P_i may be overwritten only once PV_i(j-1) has read it
       if (!o_ready) {
         if (!mbar_wait_warp(&o_done[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
@@ -397,15 +451,23 @@ extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, 
   a.ctl = make_ctl();
   const long long grid = (long long)a.nqb * heads * batches;
   if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
-  static bool attr_set[64] = {};
-  if (di.device < 64 && !attr_set[di.device]) {
-    int rc = check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             AttnSmem::TOTAL),
+  // Share of exponentials computed on the FMA pipe (pairs per 8); the
+  // QVGGT_ATTN_POLY environment variable (0..4) overrides the default.
+  static int poly = -1;
+  if (poly < 0) {
+    const char* e = getenv("QVGGT_ATTN_POLY");
+    poly = (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 0;
+  }
+  auto kfn = poly == 0 ? attn_fwd_kernel<0> : poly == 1 ? attn_fwd_kernel<1> : poly == 2 ? attn_fwd_kernel<2>
+           : poly == 3 ? attn_fwd_kernel<3> : attn_fwd_kernel<4>;
+  static bool attr_set[64][5] = {};
+  if (di.device < 64 && !attr_set[di.device][poly]) {
+    int rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::TOTAL),
                         "cudaFuncSetAttribute(attention)");
     if (rc) return rc;
-    attr_set[di.device] = true;
+    attr_set[di.device][poly] = true;
   }
-  attn_fwd_kernel<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK, tmV, a);
+  kfn<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK, tmV, a);
   int rc = check_cuda(cudaGetLastError(), "attention launch");
   if (!rc) count_launch(1);
   return rc;

@@ -192,6 +192,30 @@ int qvggt_w4a16_linear_ex(const void* in_feats, int64_t lda, const void* qweight
   return rc;
 }
 
+int qvggt_qkv_rope_linear(const void* in_feats, int32_t weight_kind, const void* qweight, const void* scales,
+                          const void* scaled_zeros, int64_t gpad, int32_t group_size, const void* bias, void* q_out,
+                          void* kv_out, int64_t M, int64_t K, int32_t dim, int64_t token_offset,
+                          int32_t tokens_per_frame, int32_t patch_start, int32_t grid_w, const void* cos_tab,
+                          const void* sin_tab, int32_t max_pos, int32_t qk_norm, const void* qn_w, const void* qn_b,
+                          const void* kn_w, const void* kn_b, float eps, void* stream) {
+  if (weight_kind != 0 && weight_kind != 1) return set_error(QVGGT_ERR_INVALID, "qkv_rope_linear: weight_kind");
+  if (qk_norm && (!qn_w || !qn_b || !kn_w || !kn_b))
+    return set_error(QVGGT_ERR_INVALID, "qkv_rope_linear: qk_norm needs weights");
+  GemmLaunch L;
+  L.mode = weight_kind == 0 ? B_W4 : B_F16;
+  L.epi = EPI_QKV_ROPE;
+  L.a = in_feats; L.lda = K; L.b = qweight; L.scales = scales; L.zeros = scaled_zeros; L.gpad = gpad;
+  L.group_size = group_size; L.bias = bias; L.out = q_out; L.ldo = dim;
+  L.M = M; L.N = 3LL * dim; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  L.rope.q_out = q_out; L.rope.kv_out = kv_out; L.rope.dim = dim; L.rope.cos_tab = cos_tab; L.rope.sin_tab = sin_tab;
+  L.rope.max_pos = max_pos; L.rope.tokens_per_frame = tokens_per_frame; L.rope.patch_start = patch_start;
+  L.rope.grid_w = grid_w; L.rope.token_offset = token_offset; L.rope.eps = eps;
+  if (qk_norm) { L.rope.qn_w = qn_w; L.rope.qn_b = qn_b; L.rope.kn_w = kn_w; L.rope.kn_b = kn_b; }
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
 int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, const void* bias, void* out,
                         int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
                         const void* gamma, void* stream) {

@@ -62,8 +62,91 @@ struct GemmArgs {
   const __half* gamma;
   const __half* wscale;
   const __half* ascale;
+  RopeEpi rope;
   Ctl ctl;
 };
+
+// EPI_QKV_ROPE for one 64-wide head of one row: y = half(half(acc) + bias),
+// then for q / k heads the optional per-head LayerNorm and the 2-D RoPE of the
+// VGGT aggregator (dims 0..31 rotated by the patch row, 32..63 by the patch
+// column, rotate-half pairs i <-> i+16, h(h(x*cos) + h(rot*sin))), stored to
+// q_out or kv_out.
+__device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, int col0, const uint32_t (&r)[64]) {
+  const RopeEpi& R = g.rope;
+  const int region = col0 / R.dim;           // 0 = q, 1 = k, 2 = v
+  const int hcol = col0 - region * R.dim;    // column of the head inside its region
+  float y[64];
+  const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 bu = g.bias ? __ldg(bp + j) : make_uint4(0, 0, 0, 0);
+    const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 b = unpack_half2(b4[e]);
+      y[8 * j + 2 * e] = round_f16(round_f16(__uint_as_float(r[8 * j + 2 * e])) + b.x);
+      y[8 * j + 2 * e + 1] = round_f16(round_f16(__uint_as_float(r[8 * j + 2 * e + 1])) + b.y);
+    }
+  }
+  __half* dst;
+  if (region == 0) {
+    dst = reinterpret_cast<__half*>(R.q_out) + (long long)row * R.dim + hcol;
+  } else {
+    dst = reinterpret_cast<__half*>(R.kv_out) + (long long)row * 2 * R.dim + (region - 1) * R.dim + hcol;
+  }
+  if (region < 2) {
+    const __half* nw = reinterpret_cast<const __half*>(region == 0 ? R.qn_w : R.kn_w);
+    const __half* nb = reinterpret_cast<const __half*>(region == 0 ? R.qn_b : R.kn_b);
+    if (nw) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) s += y[i];
+      const float mean = s * (1.f / 64.f);
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) q = fmaf(y[i] - mean, y[i] - mean, q);
+      const float rstd = rsqrtf(q * (1.f / 64.f) + R.eps);
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        y[i] = round_f16(fmaf((y[i] - mean) * rstd, __half2float(__ldg(nw + i)), __half2float(__ldg(nb + i))));
+    }
+    const int p = (int)(((long long)row + R.token_offset) % R.tokens_per_frame);
+    int py = 0, px = 0;
+    if (p >= R.patch_start) {
+      const int q = p - R.patch_start;
+      py = min(q / R.grid_w + 1, R.max_pos - 1);
+      px = min(q % R.grid_w + 1, R.max_pos - 1);
+    }
+    const __half* ct = reinterpret_cast<const __half*>(R.cos_tab);
+    const __half* st = reinterpret_cast<const __half*>(R.sin_tab);
+    // The tables hold each angle twice (columns i and i+16 are equal), so the
+    // pair (i, i+16) shares one cos / sin: rotate it in place.
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int pp = half ? px : py;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 cu = __ldg(reinterpret_cast<const uint4*>(ct + pp * 32) + j);
+        const uint4 su = __ldg(reinterpret_cast<const uint4*>(st + pp * 32) + j);
+        const uint32_t c4[4] = {cu.x, cu.y, cu.z, cu.w}, s4[4] = {su.x, su.y, su.z, su.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 32 * half + 8 * j + e;
+          const float2 c2 = unpack_half2(c4[e / 2]), s2 = unpack_half2(s4[e / 2]);
+          const float cs = (e & 1) ? c2.y : c2.x, sn = (e & 1) ? s2.y : s2.x;
+          const float a = y[i], bq = y[i + 16];
+          y[i] = round_f16(round_f16(a * cs) + round_f16(-bq * sn));
+          y[i + 16] = round_f16(round_f16(bq * cs) + round_f16(a * sn));
+        }
+      }
+    }
+  }
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    d4[j] = make_uint4(pack_half2(y[8 * j], y[8 * j + 1]), pack_half2(y[8 * j + 2], y[8 * j + 3]),
+                       pack_half2(y[8 * j + 4], y[8 * j + 5]), pack_half2(y[8 * j + 6], y[8 * j + 7]));
+}
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
@@ -341,12 +424,23 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
       tc_fence_after();
       const int row = m_blk * BM + q * 32 + lane;
       const uint32_t tbase = tmem_addr(tmem_base, q * 32, acc * BN);
+      if (MODE != B_I8 && g.epi == EPI_QKV_ROPE) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tbase + c * 16, r);
-        tmem_ld_wait();
-        if (row < g.M) epilogue16<MODE>(g, row, n_blk * BN + c * 16, r);
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t r[64];
+          tmem_ld32(tbase + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld32(tbase + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_ld_wait();
+          if (row < g.M) epilogue_qkv_head(g, row, n_blk * BN + c * 64, r);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+          tmem_ld_wait();
+          if (row < g.M) epilogue16<MODE>(g, row, n_blk * BN + c * 16, r);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -456,6 +550,7 @@ int launch_gemm(const GemmLaunch& L) {
   g.gamma = reinterpret_cast<const __half*>(L.gamma);
   g.wscale = reinterpret_cast<const __half*>(L.wscale);
   g.ascale = reinterpret_cast<const __half*>(L.ascale);
+  g.rope = L.rope;
   g.ctl = make_ctl();
   if (g.num_tiles == 0) return QVGGT_OK;
 
@@ -493,6 +588,16 @@ int gemm_launch(const GemmLaunch& L) {
     if (!aligned16(L.scales) || !aligned16(L.zeros)) return set_error(QVGGT_ERR_ALIGN, "gemm: scales not aligned");
   }
   if (L.epi == EPI_RESID && (!L.resid || !L.gamma)) return set_error(QVGGT_ERR_INVALID, "gemm: residual needs resid+gamma");
+  if (L.epi == EPI_QKV_ROPE) {
+    const RopeEpi& R = L.rope;
+    if (L.mode == B_I8 || R.dim <= 0 || R.dim % 64 || L.N != 3 * R.dim || !R.q_out || !R.kv_out || !R.cos_tab ||
+        !R.sin_tab || R.max_pos <= 0 || R.tokens_per_frame <= 0 || R.grid_w <= 0 || R.patch_start < 0)
+      return set_error(QVGGT_ERR_INVALID, "gemm: bad qkv/rope epilogue arguments");
+    if ((R.qn_w != nullptr) != (R.kn_w != nullptr) || (R.qn_w && (!R.qn_b || !R.kn_b)))
+      return set_error(QVGGT_ERR_INVALID, "gemm: qk-norm needs all four weight vectors");
+    if (!aligned16(R.q_out) || !aligned16(R.kv_out) || !aligned16(R.cos_tab) || !aligned16(R.sin_tab))
+      return set_error(QVGGT_ERR_ALIGN, "gemm: rope epilogue tensors must be 16-byte aligned");
+  }
   if (L.mode == B_I8 && L.epi != EPI_I32 && (!L.wscale || !L.ascale)) return set_error(QVGGT_ERR_INVALID, "gemm: w8a8 needs scales");
   if (L.M == 0) return QVGGT_OK;
 

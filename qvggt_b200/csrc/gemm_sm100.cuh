@@ -7,7 +7,26 @@
 namespace qv {
 
 enum GemmMode { B_W4 = 0, B_F16 = 1, B_I8 = 2 };
-enum GemmEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_I32 = 3 };
+enum GemmEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_I32 = 3, EPI_QKV_ROPE = 4 };
+
+// EPI_QKV_ROPE: the output columns are [q | k | v] (each `dim` wide, heads of
+// 64); q and k get (optional per-head LayerNorm and) VGGT 2-D RoPE, q goes to
+// q_out [M, dim], k and v to kv_out [M, 2*dim].
+struct RopeEpi {
+  void* q_out = nullptr;
+  void* kv_out = nullptr;
+  int dim = 1024;
+  const void* cos_tab = nullptr;   // fp16 [max_pos, 32]
+  const void* sin_tab = nullptr;
+  int max_pos = 0;
+  int tokens_per_frame = 1374, patch_start = 5, grid_w = 37;
+  long long token_offset = 0;
+  const void* qn_w = nullptr;      // fp16 [64] each, all null = no qk-norm
+  const void* qn_b = nullptr;
+  const void* kn_w = nullptr;
+  const void* kn_b = nullptr;
+  float eps = 1e-6f;
+};
 
 struct GemmLaunch {
   int mode = B_W4;
@@ -28,6 +47,7 @@ struct GemmLaunch {
   const void* wscale = nullptr;  // B_I8: fp16 [N]
   const void* ascale = nullptr;  // B_I8: fp16 [M]
   long long M = 0, N = 0, K = 0;
+  RopeEpi rope;                  // EPI_QKV_ROPE only
   bool force_bn128 = false;
   cudaStream_t stream = nullptr;
 };

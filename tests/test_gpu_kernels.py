@@ -320,3 +320,27 @@ def test_bad_arguments_raise():
         eng.gemm_forward_cuda_new(x.cpu(), qw, s, s)    # no CPU path
     with pytest.raises(RuntimeError):
         eng.gemv_forward_cuda_new(torch.zeros(17, 128, dtype=torch.float16, device=DEV), qw, s, s, 17, 128, 128, 128)
+
+
+@pytest.mark.parametrize("kind,qk_norm", [("w4", False), ("w4", True), ("f16", False)])
+def test_qkv_rope_linear_matches_separate_path(kind, qk_norm):
+    """The qkv GEMM with the split + 2-D RoPE fused into its epilogue equals the
+    separate GEMM(+bias) -> qkv_rope2d path bit for bit (same roundings)."""
+    from qvggt_b200 import awq_inference_engine as eng
+    from qvggt_b200.aggregator import AggConfig, rope_tables
+    from qvggt_b200.synthetic import random_linear
+    cfg = AggConfig()
+    gen = torch.Generator(device=DEV).manual_seed(17)
+    lin = random_linear(1024, 3072, gen, DEV, kind)
+    T = 2 * 1374 + 100                                    # ragged: not a whole number of frames or tiles
+    x = torch.randn(T, 1024, dtype=torch.float16, device=DEV)
+    cos_t, sin_t = rope_tables(cfg, DEV)
+    qn = None
+    if qk_norm:
+        qn = tuple(t.to(DEV) for t in ((1 + 0.1 * torch.randn(64)).half(), (0.1 * torch.randn(64)).half(),
+                                       (1 + 0.1 * torch.randn(64)).half(), (0.1 * torch.randn(64)).half()))
+    q1, kv1 = eng.qkv_rope_linear(x, lin, 16, cos_t, sin_t, qk_norm=qn)
+    qkv = lin(x)
+    q2, kv2 = eng.qkv_rope2d(qkv, 16, cos_t, sin_t, qk_norm=qn)
+    assert torch.equal(q1, q2)
+    assert torch.equal(kv1, kv2)
