@@ -117,6 +117,13 @@ int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const void* scal
 int qvggt_w8a8_gemm(const int8_t* in, const int8_t* w, const void* wscales, const void* ascales, const void* bias,
                     void* out, int64_t M, int64_t N, int64_t K, void* stream);
 
+/* The W8A8 GEMM of a VGGT block with the LayerScale residual fused:
+ * resid[M, N] += half(half(y) * gamma), y as in qvggt_w8a8_gemm (bias may be
+ * NULL).  New entry point (the reference has no caller of its W8A8 GEMM). */
+int qvggt_w8a8_gemm_residual(const int8_t* in, const int8_t* w, const void* wscales, const void* ascales,
+                             const void* bias, const void* gamma, void* resid, int64_t M, int64_t N, int64_t K,
+                             void* stream);
+
 /* Raw int32 accumulators acc[M, N] of the same GEMM (for bit-exact checks).
  * No reference counterpart (the reference never exposes its accumulators). */
 int qvggt_i8_gemm_i32(const int8_t* in, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,

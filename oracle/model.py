@@ -85,6 +85,13 @@ class QLinear:
             return y.reshape(*x.shape[:-1], -1)
         raise ValueError(self.kind)
 
+    def w8a8(self, xq, xs) -> torch.Tensor:
+        """int8 activations [T, K] + per-token fp16 scales -> fp16 [T, N]
+        (the reference's fused-bias W8A8 GEMM epilogue)."""
+        from . import w8a8 as ow
+        return torch.from_numpy(ow.w8a8_gemm(np.asarray(xq), np.asarray(self.w8), np.asarray(self.wscale),
+                                             np.asarray(xs), None if self.bias is None else np.asarray(self.bias)))
+
 
 def random_w4_linear(K: int, N: int, gen: np.random.Generator, group_size: int = 128,
                      w_std: float = 0.02) -> QLinear:
@@ -159,6 +166,33 @@ def block_forward(x: torch.Tensor, blk: dict, pos: torch.Tensor | None, heads: i
     f = gelu_erf(blk["fc1"](h2))
     y2 = blk["fc2"](f)
     return r16(x.float() + r16(y2.float() * torch.as_tensor(blk["ls2"]).float()).float())
+
+
+def block_forward_w8a8(x: torch.Tensor, blk: dict, pos: torch.Tensor, heads: int = 16,
+                       eps: float = 1e-6) -> torch.Tensor:
+    """W8A8 block over x [B, L, C], the chain the
+    reference's W8A8 kernels imply (``csrc/w8a8``): rms_norm_general ->
+    int8 GEMM + bias -> 2-D RoPE -> attention -> invoke_quant -> int8 GEMM +
+    bias -> LayerScale residual -> rms_norm_general -> int8 GEMM + bias ->
+    gelu_and_quant (tanh GELU) -> int8 GEMM + bias -> LayerScale residual."""
+    from . import w8a8 as ow
+    B, L, C = x.shape
+    hd = C // heads
+    xf = x.reshape(B * L, C)
+    q8, s = ow.rms_norm_general(xf.numpy(), np.asarray(blk["norm1_w"]), np.asarray(blk["norm1_b"]), eps)
+    qkv = blk["qkv"].w8a8(q8, s).reshape(B, L, 3, heads, hd).permute(2, 0, 3, 1, 4)
+    q = rope.rope2d(qkv[0], pos)
+    k = rope.rope2d(qkv[1], pos)
+    o = sdpa(q, k, qkv[2]).transpose(1, 2).reshape(B * L, C)
+    oq, os_ = ow.invoke_quant(o.numpy())
+    y = blk["proj"].w8a8(oq, os_)
+    xf = r16(xf.float() + r16(y.float() * torch.as_tensor(blk["ls1"]).float()).float())
+    q8, s = ow.rms_norm_general(xf.numpy(), np.asarray(blk["norm2_w"]), np.asarray(blk["norm2_b"]), eps)
+    f = blk["fc1"].w8a8(q8, s)
+    fq, fs, _ = ow.gelu_and_quant(f.numpy())
+    y2 = blk["fc2"].w8a8(fq, fs)
+    xf = r16(xf.float() + r16(y2.float() * torch.as_tensor(blk["ls2"]).float()).float())
+    return xf.reshape(B, L, C)
 
 
 def block_pair_forward(tokens: torch.Tensor, frame_blk: dict, global_blk: dict,

@@ -32,6 +32,7 @@ SIGNATURES = {
     "qvggt_w4a16_gemv": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
     "qvggt_w8a8_gemm": [vp, vp, vp, vp, vp, vp, i64, i64, i64, vp],
     "qvggt_i8_gemm_i32": [vp, vp, vp, i64, i64, i64, vp],
+    "qvggt_w8a8_gemm_residual": [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp],
     "qvggt_invoke_quant": [vp, vp, vp, i64, i64, vp],
     "qvggt_layernorm_quant": [vp, vp, vp, vp, vp, i64, i64, f32, i32, vp],
     "qvggt_gelu_quant": [vp, vp, vp, vp, i64, i64, vp],

@@ -66,6 +66,8 @@ class Linear:
         if kind == "w4":
             self.out_features = self.qweight.shape[0] * 4
             self.in_features = self.qweight.shape[1]
+        elif kind == "w8":   # int8 weight [N, K] + fp16 per-channel scale `wscale` [N]
+            self.out_features, self.in_features = self.w8.shape
         else:
             self.out_features, self.in_features = self.weight.shape
 
@@ -125,8 +127,13 @@ def rope_tables(cfg: AggConfig, device):
 class Workspace:
     """Activation buffers for T local tokens (allocated once, reused by every block)."""
 
-    def __init__(self, T_local: int, T_global: int, cfg: AggConfig, device):
+    def __init__(self, T_local: int, T_global: int, cfg: AggConfig, device, w8a8: bool = False):
         C = cfg.dim
+        if w8a8:   # int8 activations + per-token fp16 scales of the W8A8 chain
+            self.xq = torch.empty(T_local, C, dtype=torch.int8, device=device)
+            self.xs = torch.empty(T_local, dtype=F16, device=device)
+            self.mq = torch.empty(T_local, cfg.mlp_ratio * C, dtype=torch.int8, device=device)
+            self.ms = torch.empty(T_local, dtype=F16, device=device)
         self.h = torch.empty(T_local, C, dtype=F16, device=device)
         self.qkv = torch.empty(T_local, 3 * C, dtype=F16, device=device)
         self.q = torch.empty(T_local, C, dtype=F16, device=device)
@@ -156,7 +163,8 @@ class AggregatorRunner:
         self.device = torch.device(device)
         P = cfg.tokens_per_frame
         self.T = frames_local * P
-        self.ws = Workspace(self.T, self.T * world, cfg, self.device)
+        self.w8a8 = any(b.qkv.kind == "w8" for b in list(frame_blocks) + list(global_blocks))
+        self.ws = Workspace(self.T, self.T * world, cfg, self.device, self.w8a8)
         self.cos, self.sin = rope_tables(cfg, self.device)
         # When a list: (start event, end event, algorithmic FLOP) of every
         # global-attention launch is appended (CUDA events on the current stream).
@@ -170,6 +178,8 @@ class AggregatorRunner:
         cfg, ws = self.cfg, self.ws
         P = cfg.tokens_per_frame
         C = cfg.dim
+        if blk.qkv.kind == "w8":
+            return self.block_w8a8(x, blk, kind)
         eng.layernorm(x, blk.norm1_w, blk.norm1_b, cfg.eps, out=ws.h)
         if not rope:
             blk.qkv(ws.h, out=ws.qkv)
@@ -206,6 +216,42 @@ class AggregatorRunner:
         eng.layernorm(x, blk.norm2_w, blk.norm2_b, cfg.eps, out=ws.h)
         blk.fc1(ws.h, out=ws.mlp, act="gelu")
         blk.fc2(ws.mlp, residual=x, gamma=blk.ls2)
+
+    def _attend(self, kind: str, kv_dst: torch.Tensor) -> None:
+        cfg, ws = self.cfg, self.ws
+        if kind == "global":
+            if self.world > 1:
+                kv, Lkv = gather_kv(ws.kv_global, self.T, self.rank, self.group), self.T * self.world
+            else:
+                kv, Lkv = ws.kv_local, self.T
+            eng.attention(ws.q, kv, cfg.heads, 1, self.T, Lkv, out=ws.attn)
+        else:
+            eng.attention(ws.q, ws.kv_local, cfg.heads, self.S_local, cfg.tokens_per_frame, cfg.tokens_per_frame,
+                          out=ws.attn)
+
+    def block_w8a8(self, x: torch.Tensor, blk: Block, kind: str) -> None:
+        """W8A8 block, the chain the reference's W8A8 ops
+        imply: LayerNorm + per-token int8 (rms_norm_general) -> int8 GEMM
+        (+bias) -> 2-D RoPE -> attention -> per-token int8 (invoke_quant) ->
+        int8 GEMM (+bias, LayerScale residual) -> LayerNorm + int8 -> int8 GEMM
+        (+bias) -> tanh-GELU + int8 (gelu_and_quant) -> int8 GEMM (+bias,
+        LayerScale residual)."""
+        cfg, ws = self.cfg, self.ws
+        P = cfg.tokens_per_frame
+        eng.rms_norm_general(ws.xq, x, blk.norm1_w, blk.norm1_b, ws.xs, cfg.eps, True)
+        q = blk.qkv
+        eng.w8a8_gemm_fuse_bias_forward_cuda(ws.xq, q.w8, q.wscale, ws.xs, ws.qkv, q.bias)
+        glob = kind == "global"
+        kv_dst = kv_slice(ws.kv_global, self.T, self.rank) if (glob and self.world > 1) else ws.kv_local
+        eng.qkv_rope2d(ws.qkv, cfg.heads, self.cos, self.sin, P, cfg.patch_start, cfg.grid_w, 0, q_out=ws.q,
+                       kv_out=kv_dst, qk_norm=blk.qk_norm, eps=cfg.eps)
+        self._attend(kind, kv_dst)
+        eng.invoke_quant(ws.xq, ws.attn, ws.xs)
+        eng.w8a8_gemm_residual(ws.xq, blk.proj.w8, blk.proj.wscale, ws.xs, blk.proj.bias, blk.ls1, x)
+        eng.rms_norm_general(ws.xq, x, blk.norm2_w, blk.norm2_b, ws.xs, cfg.eps, True)
+        eng.w8a8_gemm_fuse_bias_forward_cuda(ws.xq, blk.fc1.w8, blk.fc1.wscale, ws.xs, ws.mlp, blk.fc1.bias)
+        eng.gelu_and_quant(ws.mq, ws.mlp, ws.ms, ws.mlp)          # tmp written in place over the fc1 output
+        eng.w8a8_gemm_residual(ws.mq, blk.fc2.w8, blk.fc2.wscale, ws.ms, blk.fc2.bias, blk.ls2, x)
 
     def forward(self, tokens: torch.Tensor, keep: tuple[int, ...] = ()) -> dict:
         """tokens [S_local, P, C] fp16 (modified in place).  Runs every pair;

@@ -218,6 +218,19 @@ def w8a8_gemm_fuse_bias_forward_cuda(in_feats, kernel, wscales, ascales, out_fea
     _w8a8("w8a8_gemm_fuse_bias_forward_cuda", in_feats, kernel, wscales, ascales, out_feats, bias)
 
 
+def w8a8_gemm_residual(in_feats, kernel, wscales, ascales, bias, gamma, residual):
+    """residual += half(half(W8A8 GEMM(+bias)) * gamma) (LayerScale residual fused)."""
+    name = "w8a8_gemm_residual"
+    dev = _check_cuda(name, in_feats, kernel, wscales, ascales, bias, gamma, residual)
+    _contig(name, in_feats, kernel, wscales, ascales, bias, gamma, residual)
+    M, K = in_feats.shape[0], in_feats.shape[1]
+    N = kernel.shape[0]
+    with _Dev(dev):
+        _lib.call("qvggt_w8a8_gemm_residual", _ptr(in_feats), _ptr(kernel), _ptr(wscales), _ptr(ascales), _ptr(bias),
+                  _ptr(gamma), _ptr(residual), M, N, K, _stream(in_feats))
+    return residual
+
+
 def i8_gemm_i32(in_feats, kernel):
     """Raw int32 accumulators of the int8 GEMM (for bit-exact checks)."""
     name = "i8_gemm_i32"

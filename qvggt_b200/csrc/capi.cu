@@ -244,6 +244,20 @@ int qvggt_w8a8_gemm(const int8_t* in, const int8_t* w, const void* wscales, cons
   return rc;
 }
 
+int qvggt_w8a8_gemm_residual(const int8_t* in, const int8_t* w, const void* wscales, const void* ascales,
+                             const void* bias, const void* gamma, void* resid, int64_t M, int64_t N, int64_t K,
+                             void* stream) {
+  GemmLaunch L;
+  L.mode = B_I8;
+  L.epi = EPI_RESID;
+  L.a = in; L.lda = K; L.b = w; L.bias = bias; L.out = resid; L.ldo = N; L.resid = resid; L.ldr = N;
+  L.gamma = gamma; L.wscale = wscales; L.ascale = ascales;
+  L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
 int qvggt_i8_gemm_i32(const int8_t* in, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                       void* stream) {
   GemmLaunch L;

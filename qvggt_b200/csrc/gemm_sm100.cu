@@ -188,6 +188,24 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, int row, int col, 
         y[2 * i + 1] = __fmul_rn(__int2float_rn((int)r[2 * i + 1]), __fmul_rn(ws.y, as));
       }
     }
+    if (g.epi == EPI_RESID) {
+      // out = resid + half(half(y) * gamma): the W8A8 linear's fp16 output,
+      // then the LayerScale residual add of the block
+      const uint4* gp = reinterpret_cast<const uint4*>(g.gamma + col);
+      const uint4* rp = reinterpret_cast<const uint4*>(g.resid + (long long)row * g.ldr + col);
+      uint32_t gu[8], ru[8];
+      *reinterpret_cast<uint4*>(&gu[0]) = __ldg(gp);
+      *reinterpret_cast<uint4*>(&gu[4]) = __ldg(gp + 1);
+      *reinterpret_cast<uint4*>(&ru[0]) = rp[0];
+      *reinterpret_cast<uint4*>(&ru[4]) = rp[1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 gm = unpack_half2(gu[i]);
+        const float2 x = unpack_half2(ru[i]);
+        y[2 * i] = x.x + round_f16(round_f16(y[2 * i]) * gm.x);
+        y[2 * i + 1] = x.y + round_f16(round_f16(y[2 * i + 1]) * gm.y);
+      }
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < 16; ++i) y[i] = round_f16(__uint_as_float(r[i]));

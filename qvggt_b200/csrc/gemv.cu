@@ -12,7 +12,7 @@
 namespace qv {
 namespace {
 
-template <int MT>
+template <int MT, int MAXIT>
 __global__ void __launch_bounds__(128) gemv_w4_kernel(const __half* __restrict__ x, const uint16_t* __restrict__ qw,
                                                       const __half* __restrict__ scales,
                                                       const __half* __restrict__ zeros, const __half* __restrict__ bias,
@@ -31,14 +31,29 @@ __global__ void __launch_bounds__(128) gemv_w4_kernel(const __half* __restrict__
   const int ci = (lane & 7) >> 1;   // constant over iterations (stride is a multiple of 128 B)
   const int h = lane & 1;
   const __half2 magic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  for (int off = (warp * 32 + lane) * 16; off < row_bytes; off += 128 * 16) {
+  // Issue every weight (and scale / zero) load of this thread before any math,
+  // so up to MAXIT 16-byte loads per thread are in flight at once.
+  uint4 wvs[MAXIT];
+  __half ss[MAXIT], zs[MAXIT];
+  const int off0 = (warp * 32 + lane) * 16;
+#pragma unroll
+  for (int it = 0; it < MAXIT; ++it) {
+    const int off = off0 + it * 128 * 16;
+    if (off < row_bytes) {
+      wvs[it] = __ldg(reinterpret_cast<const uint4*>(row + off));
+      const int grp = (64 * (off >> 7) + 32 * h) / G;
+      ss[it] = scales[(size_t)grp * N + 4 * g + ci];
+      zs[it] = zeros[(size_t)grp * N + 4 * g + ci];
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < MAXIT; ++it) {
+    const int off = off0 + it * 128 * 16;
+    if (off >= row_bytes) break;
     const int c = off >> 7;
     const int k0 = 64 * c + 32 * h;
-    uint4 wv = __ldg(reinterpret_cast<const uint4*>(row + off));
-    const int grp = k0 / G;
-    const __half s = scales[(size_t)grp * N + 4 * g + ci];
-    const __half z = zeros[(size_t)grp * N + 4 * g + ci];
-    const __half2 s2 = __half2half2(s), z2 = __half2half2(z);
+    const uint4 wv = wvs[it];
+    const __half2 s2 = __half2half2(ss[it]), z2 = __half2half2(zs[it]);
     const uint32_t xs[4] = {wv.x, wv.y, wv.z, wv.w};
     // w[q][u] covers k = k0 + 8q + 2u, +1
     float2 w[4][4];
@@ -124,11 +139,22 @@ extern "C" int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const
                                 static_cast<const __half*>(bias), static_cast<__half*>(out), (int)m, (int)N, (int)K,
                                 group_size);
   };
-  if (m <= 1) args(gemv_w4_kernel<1>);
-  else if (m <= 2) args(gemv_w4_kernel<2>);
-  else if (m <= 4) args(gemv_w4_kernel<4>);
-  else if (m <= 8) args(gemv_w4_kernel<8>);
-  else args(gemv_w4_kernel<16>);
+  // 16-byte chunks per thread: a packed row is 2K bytes, a CTA covers 2 KB per pass
+  const int iters = (int)((K * 2 + 2047) / 2048);
+  auto by_m = [&](auto mt) {
+    constexpr int MT = decltype(mt)::value;
+    if (iters <= 1) args(gemv_w4_kernel<MT, 1>);
+    else if (iters <= 2) args(gemv_w4_kernel<MT, 2>);
+    else if (iters <= 4) args(gemv_w4_kernel<MT, 4>);
+    else if (iters <= 8) args(gemv_w4_kernel<MT, 8>);
+    else args(gemv_w4_kernel<MT, 16>);
+  };
+  if (K > 16384) return set_error(QVGGT_ERR_UNSUPPORTED, "gemv: K=%lld > 16384", (long long)K);
+  if (m <= 1) by_m(std::integral_constant<int, 1>());
+  else if (m <= 2) by_m(std::integral_constant<int, 2>());
+  else if (m <= 4) by_m(std::integral_constant<int, 4>());
+  else if (m <= 8) by_m(std::integral_constant<int, 8>());
+  else by_m(std::integral_constant<int, 16>());
   int rc = check_cuda(cudaGetLastError(), "gemv launch");
   if (rc == QVGGT_OK) count_launch(1);
   return rc;

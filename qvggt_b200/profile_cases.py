@@ -1,0 +1,117 @@
+"""Small, fixed workloads of single kernels for profiling (ncu) and timing.
+
+    python -m qvggt_b200.profile_cases attn  [L] [batches]   # flash attention, 16 heads x 64
+    python -m qvggt_b200.profile_cases gemm  f16|w4|w8 [M]    # tcgen05 GEMM, N=4096 K=1024
+    python -m qvggt_b200.profile_cases mem                    # LayerNorm, invoke_quant, GEMV
+    python -m qvggt_b200.profile_cases time                   # CUDA-event timings of all of the above
+
+Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
+launch) on seeded synthetic data sized above the 126 MB L2 where it matters.
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from . import _lib
+from . import awq_inference_engine as eng
+
+
+def _w4(N, K, seed=1):
+    from .synthetic import quantize_w4
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn(N, K, generator=g, device="cuda") * 0.02
+    return quantize_w4(w, 128)
+
+
+def attn(L=16384, b=1, reps=2):
+    C = 1024
+    q = torch.randn(b * L, C, dtype=torch.float16, device="cuda")
+    kv = torch.randn(b * L, 2 * C, dtype=torch.float16, device="cuda")
+    out = torch.empty(b * L, C, dtype=torch.float16, device="cuda")
+    fn = lambda: eng.attention(q, kv, 16, b, L, L, out=out)
+    for _ in range(reps):
+        fn()
+    return fn, 4.0 * b * L * L * C
+
+
+def gemm(mode="f16", M=32768, N=4096, K=1024, reps=2):
+    x = torch.randn(M, K, dtype=torch.float16, device="cuda")
+    if mode == "f16":
+        w = torch.randn(N, K, dtype=torch.float16, device="cuda") * 0.02
+        out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        fn = lambda: eng.f16_linear(x, w, out=out)
+    elif mode == "w4":
+        qw, s, z = _w4(N, K)
+        fn = lambda: eng.gemm_forward_cuda_new(x, qw, s, z)
+    else:
+        a8 = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+        w8 = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+        ws = torch.rand(N, device="cuda").half() * 1e-3
+        as_ = torch.rand(M, device="cuda").half() * 1e-2
+        out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        fn = lambda: eng.w8a8_gemm_forward_cuda(a8, w8, ws, as_, out)
+    for _ in range(reps):
+        fn()
+    return fn, 2.0 * M * N * K
+
+
+def mem(reps=2):
+    T = 43968
+    x = torch.randn(T, 1024, dtype=torch.float16, device="cuda")
+    w1 = torch.ones(1024, dtype=torch.float16, device="cuda")
+    q8 = torch.empty(T, 1024, dtype=torch.int8, device="cuda")
+    sc = torch.empty(T, dtype=torch.float16, device="cuda")
+    qw, s, z = _w4(4096, 4096)
+    x1 = torch.randn(1, 4096, dtype=torch.float16, device="cuda")
+    fns = {
+        "layernorm [43968,1024]": (lambda: eng.layernorm(x, w1, w1), 2 * T * 1024 * 2),
+        "invoke_quant [43968,1024]": (lambda: eng.invoke_quant(q8, x, sc), T * 1024 * 3 + 2 * T),
+        "gemv m=1 N=K=4096": (lambda: eng.gemv_forward_cuda_new(x1, qw, s, z, 1, 4096, 4096, 128),
+                              4096 * 4096 // 2 + 2 * s.numel() * 2 + 4096 * 4),
+    }
+    for f, _ in fns.values():
+        for _ in range(reps):
+            f()
+    return fns
+
+
+def _time(fn, iters=20):
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters / 1e3
+
+
+def main(argv):
+    _lib.load()
+    what = argv[0] if argv else "time"
+    if what == "attn":
+        attn(*(int(v) for v in argv[1:3]))
+    elif what == "gemm":
+        gemm(argv[1] if len(argv) > 1 else "f16", *(int(v) for v in argv[2:3]))
+    elif what == "mem":
+        mem()
+    elif what == "time":
+        for L, b in ((16384, 1), (43968, 1), (1374, 32)):
+            fn, fl = attn(L, b)
+            t = _time(fn, 5)
+            print(f"attention L={L} b={b}: {t * 1e3:.3f} ms {fl / t / 1e12:.0f} TFLOP/s")
+        for mode in ("f16", "w4", "w8"):
+            fn, fl = gemm(mode, 43968)
+            t = _time(fn)
+            print(f"gemm {mode} M=43968 N=4096 K=1024: {t * 1e6:.1f} us {fl / t / 1e12:.0f} T(FL)OP/s")
+        for name, (fn, nbytes) in mem().items():
+            t = _time(fn, 100)
+            print(f"{name}: {t * 1e6:.2f} us {nbytes / t / 1e9:.0f} GB/s")
+    torch.cuda.synchronize()
+    print("ok", what)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])

@@ -41,6 +41,11 @@ def random_linear(K: int, N: int, gen: torch.Generator, device, kind: str = "w4"
     if kind == "w4":
         qw, st, szt = quantize_w4(w, group_size)
         return Linear("w4", bias, group_size, qweight=qw, scales=st, scaled_zeros=szt)
+    if kind == "w8":
+        # int8 symmetric per output channel, scale = max|W| / 127
+        s = (w.abs().amax(dim=1) / 127.0).to(F16)
+        q = torch.round(w / s.float()[:, None]).clamp(-128, 127).to(torch.int8).contiguous()
+        return Linear("w8", bias, w8=q, wscale=s.contiguous())
     return Linear("f16", bias, weight=w.to(F16).contiguous())
 
 

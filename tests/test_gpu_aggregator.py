@@ -54,6 +54,39 @@ def test_block_pair_matches_oracle(qk_norm, ls):
     assert d_f <= 2e-2 and d_g <= 5e-2, (d_f, d_g)
 
 
+def test_w8a8_block_pair_matches_oracle():
+    """BASELINE config 3 semantics (W8A8 linears, per-token int8 activations
+    fused into LayerNorm / GELU) at S=2: rel-L2 <= 2e-2 on the block outputs and
+    on the block updates."""
+    from qvggt_b200.aggregator import AggConfig, AggregatorRunner
+    from qvggt_b200.synthetic import random_block
+    cfg = AggConfig(layer_scale=0.3)
+    S, P, C = 2, cfg.tokens_per_frame, cfg.dim
+    gen = torch.Generator(device=DEV).manual_seed(21)
+    fb = random_block(cfg, gen, DEV, kind="w8")
+    gb = random_block(cfg, gen, DEV, kind="w8")
+    tokens = torch.randn(S, P, C, generator=torch.Generator().manual_seed(5)).half()
+    run = AggregatorRunner(cfg, [fb], [gb], S, DEV)
+    fr, gl = run.forward(tokens.to(DEV).clone())[-1]
+
+    def ob(blk):
+        def ql(l):
+            return om.QLinear("w8", w8=l.w8.cpu().numpy(), wscale=l.wscale.cpu().numpy(), bias=l.bias.cpu().numpy())
+        return dict(norm1_w=blk.norm1_w.cpu(), norm1_b=blk.norm1_b.cpu(), qkv=ql(blk.qkv), proj=ql(blk.proj),
+                    ls1=blk.ls1.cpu(), norm2_w=blk.norm2_w.cpu(), norm2_b=blk.norm2_b.cpu(), fc1=ql(blk.fc1),
+                    fc2=ql(blk.fc2), ls2=blk.ls2.cpu())
+
+    from oracle import rope as orope
+    pos = orope.patch_positions(P)
+    ref_f = om.block_forward_w8a8(tokens, ob(fb), pos)
+    ref_g = om.block_forward_w8a8(ref_f.reshape(1, S * P, C), ob(gb), pos.repeat(S, 1)).reshape(S, P, C)
+    got_f, got_g = fr.view(S, P, C).cpu(), gl.view(S, P, C).cpu()
+    assert awq.rel_l2(got_f, ref_f) <= 2e-2
+    assert awq.rel_l2(got_g, ref_g) <= 2e-2
+    assert awq.rel_l2(got_f.float() - tokens.float(), ref_f.float() - tokens.float()) <= 2e-2
+    assert awq.rel_l2(got_g.float() - ref_f.float(), ref_g.float() - ref_f.float()) <= 5e-2
+
+
 def test_two_pairs_end_to_end():
     from qvggt_b200.aggregator import AggConfig, AggregatorRunner
     from qvggt_b200.synthetic import random_aggregator_blocks
