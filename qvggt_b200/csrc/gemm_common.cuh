@@ -1,0 +1,241 @@
+// Shared pieces of the tcgen05 GEMM kernels (1-SM and 2-SM variants): the
+// argument block, the fused epilogues and the bit-exact int4 dequantisation.
+#pragma once
+
+#include "common.cuh"
+#include "gemm_sm100.cuh"
+
+namespace qv {
+namespace gemmk {
+
+struct GemmArgs {
+  int M, N, K;
+  int n_blocks, num_tiles, num_kb;
+  int group_size;
+  int epi;
+  const __half* bias;
+  __half* out;
+  long long ldo;
+  const __half* resid;
+  long long ldr;
+  const __half* gamma;
+  const __half* wscale;
+  const __half* ascale;
+  RopeEpi rope;
+  Ctl ctl;
+};
+
+// EPI_QKV_ROPE for one 64-wide head of one row: y = half(half(acc) + bias),
+// then for q / k heads the optional per-head LayerNorm and the 2-D RoPE of the
+// VGGT aggregator (dims 0..31 rotated by the patch row, 32..63 by the patch
+// column, rotate-half pairs i <-> i+16, h(h(x*cos) + h(rot*sin))), stored to
+// q_out or kv_out.
+__device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, int col0, const uint32_t (&r)[64]) {
+  const RopeEpi& R = g.rope;
+  const int region = col0 / R.dim;           // 0 = q, 1 = k, 2 = v
+  const int hcol = col0 - region * R.dim;    // column of the head inside its region
+  float y[64];
+  const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 bu = g.bias ? __ldg(bp + j) : make_uint4(0, 0, 0, 0);
+    const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 b = unpack_half2(b4[e]);
+      y[8 * j + 2 * e] = round_f16(round_f16(__uint_as_float(r[8 * j + 2 * e])) + b.x);
+      y[8 * j + 2 * e + 1] = round_f16(round_f16(__uint_as_float(r[8 * j + 2 * e + 1])) + b.y);
+    }
+  }
+  __half* dst;
+  if (region == 0) {
+    dst = reinterpret_cast<__half*>(R.q_out) + (long long)row * R.dim + hcol;
+  } else {
+    dst = reinterpret_cast<__half*>(R.kv_out) + (long long)row * 2 * R.dim + (region - 1) * R.dim + hcol;
+  }
+  if (region < 2) {
+    const __half* nw = reinterpret_cast<const __half*>(region == 0 ? R.qn_w : R.kn_w);
+    const __half* nb = reinterpret_cast<const __half*>(region == 0 ? R.qn_b : R.kn_b);
+    if (nw) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) s += y[i];
+      const float mean = s * (1.f / 64.f);
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) q = fmaf(y[i] - mean, y[i] - mean, q);
+      const float rstd = rsqrtf(q * (1.f / 64.f) + R.eps);
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        y[i] = round_f16(fmaf((y[i] - mean) * rstd, __half2float(__ldg(nw + i)), __half2float(__ldg(nb + i))));
+    }
+    const int p = (int)(((long long)row + R.token_offset) % R.tokens_per_frame);
+    int py = 0, px = 0;
+    if (p >= R.patch_start) {
+      const int q = p - R.patch_start;
+      py = min(q / R.grid_w + 1, R.max_pos - 1);
+      px = min(q % R.grid_w + 1, R.max_pos - 1);
+    }
+    const __half* ct = reinterpret_cast<const __half*>(R.cos_tab);
+    const __half* st = reinterpret_cast<const __half*>(R.sin_tab);
+    // The tables hold each angle twice (columns i and i+16 are equal), so the
+    // pair (i, i+16) shares one cos / sin: rotate it in place.
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int pp = half ? px : py;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 cu = __ldg(reinterpret_cast<const uint4*>(ct + pp * 32) + j);
+        const uint4 su = __ldg(reinterpret_cast<const uint4*>(st + pp * 32) + j);
+        const uint32_t c4[4] = {cu.x, cu.y, cu.z, cu.w}, s4[4] = {su.x, su.y, su.z, su.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 32 * half + 8 * j + e;
+          const float2 c2 = unpack_half2(c4[e / 2]), s2 = unpack_half2(s4[e / 2]);
+          const float cs = (e & 1) ? c2.y : c2.x, sn = (e & 1) ? s2.y : s2.x;
+          const float a = y[i], bq = y[i + 16];
+          y[i] = round_f16(round_f16(a * cs) + round_f16(-bq * sn));
+          y[i + 16] = round_f16(round_f16(bq * cs) + round_f16(a * sn));
+        }
+      }
+    }
+  }
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    d4[j] = make_uint4(pack_half2(y[8 * j], y[8 * j + 1]), pack_half2(y[8 * j + 2], y[8 * j + 3]),
+                       pack_half2(y[8 * j + 4], y[8 * j + 5]), pack_half2(y[8 * j + 6], y[8 * j + 7]));
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+// Epilogue for 16 consecutive columns of one row held as fp32 (or s32) bits.
+template <int MODE>
+__device__ __forceinline__ void epilogue16(const GemmArgs& g, int row, int col, const uint32_t (&r)[16]) {
+  float y[16];
+  if constexpr (MODE == B_I8) {
+    if (g.epi == EPI_I32) {
+      uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(g.out) + (long long)row * g.ldo + col);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) op[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+      return;
+    }
+    const float as = __half2float(g.ascale[row]);
+    const uint4* wsp = reinterpret_cast<const uint4*>(g.wscale + col);
+    uint32_t wsu[8];
+    *reinterpret_cast<uint4*>(&wsu[0]) = __ldg(wsp);
+    *reinterpret_cast<uint4*>(&wsu[4]) = __ldg(wsp + 1);
+    if (g.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col);
+      uint32_t bu[8];
+      *reinterpret_cast<uint4*>(&bu[0]) = __ldg(bp);
+      *reinterpret_cast<uint4*>(&bu[4]) = __ldg(bp + 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 ws = unpack_half2(wsu[i]);
+        float2 b = unpack_half2(bu[i]);
+        // (acc * ws) * as + bias, contracted (w8a8_gemm_cuda.cu:551-556)
+        y[2 * i] = __fmaf_rn(__fmul_rn(__int2float_rn((int)r[2 * i]), ws.x), as, b.x);
+        y[2 * i + 1] = __fmaf_rn(__fmul_rn(__int2float_rn((int)r[2 * i + 1]), ws.y), as, b.y);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 ws = unpack_half2(wsu[i]);
+        // acc * (ws * as) (w8a8_gemm_cuda.cu:868-873)
+        y[2 * i] = __fmul_rn(__int2float_rn((int)r[2 * i]), __fmul_rn(ws.x, as));
+        y[2 * i + 1] = __fmul_rn(__int2float_rn((int)r[2 * i + 1]), __fmul_rn(ws.y, as));
+      }
+    }
+    if (g.epi == EPI_RESID) {
+      // out = resid + half(half(y) * gamma): the W8A8 linear's fp16 output,
+      // then the LayerScale residual add of the block
+      const uint4* gp = reinterpret_cast<const uint4*>(g.gamma + col);
+      const uint4* rp = reinterpret_cast<const uint4*>(g.resid + (long long)row * g.ldr + col);
+      uint32_t gu[8], ru[8];
+      *reinterpret_cast<uint4*>(&gu[0]) = __ldg(gp);
+      *reinterpret_cast<uint4*>(&gu[4]) = __ldg(gp + 1);
+      *reinterpret_cast<uint4*>(&ru[0]) = rp[0];
+      *reinterpret_cast<uint4*>(&ru[4]) = rp[1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 gm = unpack_half2(gu[i]);
+        const float2 x = unpack_half2(ru[i]);
+        y[2 * i] = x.x + round_f16(round_f16(y[2 * i]) * gm.x);
+        y[2 * i + 1] = x.y + round_f16(round_f16(y[2 * i + 1]) * gm.y);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = round_f16(__uint_as_float(r[i]));
+    if (g.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col);
+      uint32_t bu[8];
+      *reinterpret_cast<uint4*>(&bu[0]) = __ldg(bp);
+      *reinterpret_cast<uint4*>(&bu[4]) = __ldg(bp + 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 b = unpack_half2(bu[i]);
+        y[2 * i] = round_f16(y[2 * i] + b.x);
+        y[2 * i + 1] = round_f16(y[2 * i + 1] + b.y);
+      }
+    }
+    if (g.epi == EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) y[i] = gelu_erf(y[i]);
+    } else if (g.epi == EPI_RESID) {
+      const uint4* gp = reinterpret_cast<const uint4*>(g.gamma + col);
+      const uint4* rp = reinterpret_cast<const uint4*>(g.resid + (long long)row * g.ldr + col);
+      uint32_t gu[8], ru[8];
+      *reinterpret_cast<uint4*>(&gu[0]) = __ldg(gp);
+      *reinterpret_cast<uint4*>(&gu[4]) = __ldg(gp + 1);
+      *reinterpret_cast<uint4*>(&ru[0]) = rp[0];
+      *reinterpret_cast<uint4*>(&ru[4]) = rp[1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 gm = unpack_half2(gu[i]);
+        float2 x = unpack_half2(ru[i]);
+        y[2 * i] = x.x + round_f16(y[2 * i] * gm.x);
+        y[2 * i + 1] = x.y + round_f16(y[2 * i + 1] * gm.y);
+      }
+    }
+  }
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = pack_half2(y[2 * i], y[2 * i + 1]);
+  uint4* op = reinterpret_cast<uint4*>(g.out + (long long)row * g.ldo + col);
+  op[0] = *reinterpret_cast<uint4*>(&o[0]);
+  op[1] = *reinterpret_cast<uint4*>(&o[4]);
+}
+
+// Dequantise one 16-byte chunk (4 u32 = 32 nibbles of one channel, covering
+// 32 consecutive k) into four 16-byte fp16 chunks (8 consecutive k each).
+//
+// Word w of a channel's 16-word segment holds, in nibble j, k = 32*(w/8) + w%8 + 8j
+// (relative to its 64-wide k-chunk).  The u32 formed by words (2u, 2u+1)
+// therefore holds the k pair (b, b+1), b = 2u (mod 8), in nibbles (j, j+4) for
+// each j, i.e. in the 16-bit halves of (x >> 4j) & 0x000F000F.  OR-ing the
+// exponent pattern 0x6400 makes each half the fp16 value 1024 + q exactly;
+// subtracting 1024 leaves the exact integer q; one fused multiply-add applies
+// the group scale and scaled zero (rounded once, as the reference's __hfma2).
+__device__ __forceinline__ void dequant_chunk(const uint32_t (&x)[4], __half2 s2, __half2 z2, uint4 (&out)[4]) {
+  const __half2 magic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint32_t t;
+      const uint32_t src = x[u] >> (4 * q);
+      asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(0x64006400u));
+      __half2 hq = __hsub2(*reinterpret_cast<__half2*>(&t), magic);
+      __half2 w = __hfma2(hq, s2, z2);
+      o[u] = *reinterpret_cast<uint32_t*>(&w);
+    }
+    out[q] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+
+}  // namespace gemmk
+}  // namespace qv

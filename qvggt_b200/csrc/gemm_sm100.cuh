@@ -53,5 +53,7 @@ struct GemmLaunch {
 };
 
 int gemm_launch(const GemmLaunch& L);
+// 2-SM (CTA-pair) variant for large M; called by gemm_launch after validation.
+int gemm_launch_2sm(const GemmLaunch& L);
 
 }  // namespace qv

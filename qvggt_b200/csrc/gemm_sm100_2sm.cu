@@ -1,0 +1,413 @@
+// 2-SM tcgen05 GEMM for sm_100a: the same three operand modes and fused
+// epilogues as gemm_sm100.cu, computed by CTA pairs (clusters of 2).
+//
+// A pair owns a 256 x 256 output tile.  Each CTA loads only its own 128 rows
+// of A and its own half (128 columns) of B per 128-byte k-block (W4: packs and
+// dequantises only its own 128 output channels); one thread of the even CTA
+// issues tcgen05.mma.cta_group::2 with M = 256, which reads the A rows and B
+// halves from both CTAs' shared memory and leaves each CTA's 128 rows of the
+// accumulator in its own TMEM.  Per SM this halves the B bytes pulled from L2
+// (dense / int8 modes) or the dequantisation work (W4) for the same tensor
+// work, while each SM still double-buffers its 2 x 256 accumulator columns.
+//
+// Signalling across the pair: TMA loads of both CTAs complete on the even
+// CTA's `full` barrier; the MMA commits are multicast to both CTAs' `empty`,
+// `empty_d` and `tmem_full` barriers; dequant warps and epilogue warps of both
+// CTAs arrive on the even CTA's `full_d` / `tmem_empty` barriers (mapa
+// addresses).  Every wait is bounded; both CTAs meet in a cluster barrier
+// before TMEM is freed and before either exits.  No multicast loads.
+#include "gemm_common.cuh"
+#include "gemm_sm100.cuh"
+#include "host.hpp"
+
+namespace qv {
+namespace {
+
+using namespace gemmk;
+
+constexpr int HM = 128;      // rows per CTA (the pair tile has 256)
+constexpr int KBB = 128;     // bytes of K per k-block
+constexpr int PBN = 256;     // columns of the pair tile; each CTA holds PBN/2 of B
+constexpr int HBN = PBN / 2;
+
+template <int MODE>
+struct Cfg2 {
+  static constexpr int NS = 6;
+  static constexpr int ND = (MODE == B_W4) ? 4 : 0;
+  static constexpr int A_BYTES = HM * KBB;                                  // 16 KB
+  static constexpr int B_BYTES = HBN * KBB;                                 // 16 KB: this CTA's half
+  static constexpr int BQ_BYTES = (MODE == B_W4) ? (HBN / 4) * KBB : 0;     // 4 KB packed int4
+  static constexpr int SZ_BYTES = (MODE == B_W4) ? 2 * HBN * 2 : 0;         // scales + zeros
+  // W4: two groups of HBN/32 dequantisation warps take alternate k-blocks, so
+  // two k-blocks are dequantised at once (NS and ND are even).
+  static constexpr int DQ_GROUP_WARPS = (MODE == B_W4) ? HBN / 32 : 0;
+  static constexpr int NUM_DQ_WARPS = 2 * DQ_GROUP_WARPS;
+  static constexpr int THREADS = 256 + NUM_DQ_WARPS * 32;
+  static_assert(NS % 2 == 0 && (ND % 2 == 0), "dequant groups alternate stages");
+  // barriers first, then the 1024-aligned operand stages, then a 16 KB guard
+  // so that every operand read of the pair MMA stays inside this CTA's
+  // allocation even for a full-width B tile.
+  static constexpr int OFF_BAR = 0;
+  static constexpr int NUM_BARS = 4 * NS + 2 * ND + 4 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int OFF_A = 1024;
+  static constexpr int OFF_B = OFF_A + NS * A_BYTES;                        // dense B stages / W4 packed stages
+  static constexpr int OFF_D = OFF_B + NS * ((MODE == B_W4) ? BQ_BYTES : B_BYTES);
+  static constexpr int OFF_SZ = OFF_D + ND * B_BYTES;
+  static constexpr int END = OFF_SZ + NS * SZ_BYTES;
+  static constexpr int SMEM = END + HBN * KBB + 1024;                       // + guard + alignment slack
+  static_assert(OFF_MISC + 16 <= OFF_A, "barrier region overflow");
+  static constexpr uint32_t TMEM_COLS = 2 * PBN;                            // 512: two accumulators
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
+    gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ, GemmArgs g) {
+  using C = Cfg2<MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;                   // [NS] both CTAs' TMA -> MMA (even CTA's copy is used)
+  uint64_t* empty = bars + C::NS;          // [NS] MMA -> producers (multicast)
+  uint64_t* full_b = bars + 2 * C::NS;     // [NS] local TMA -> local dequant (W4)
+  uint64_t* empty_b = bars + 3 * C::NS;    // [NS] local dequant -> local producer (W4)
+  uint64_t* full_d = bars + 4 * C::NS;     // [ND] both CTAs' dequant -> MMA (even CTA's copy)
+  uint64_t* empty_d = full_d + C::ND;      // [ND] MMA -> dequant (multicast)
+  uint64_t* tmem_full = empty_d + C::ND;   // [2] MMA -> epilogue (multicast)
+  uint64_t* tmem_empty = tmem_full + 2;    // [2] both CTAs' epilogue -> MMA (even CTA's copy)
+  uint64_t* drain_bar = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x / 2, num_clusters = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&full_b[i], 1);
+      mbar_init(&empty_b[i], C::DQ_GROUP_WARPS > 0 ? C::DQ_GROUP_WARPS : 1);
+    }
+    for (int i = 0; i < C::ND; ++i) {
+      mbar_init(&full_d[i], 2 * C::DQ_GROUP_WARPS);
+      mbar_init(&empty_d[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tmem_full[i], 1);
+      mbar_init(&tmem_empty[i], 8);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if constexpr (MODE == B_W4) {
+      tma_prefetch_desc(&tmS);
+      tma_prefetch_desc(&tmZ);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // both CTAs' barriers exist before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = g.num_kb;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters) {
+        const int m_blk = tile / g.n_blocks, n_blk = tile % g.n_blocks;
+        const int row0 = m_blk * 2 * HM + (int)rank * HM;       // this CTA's A rows
+        const int col0 = n_blk * PBN + (int)rank * HBN;         // this CTA's B columns (output channels)
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % C::NS;
+          const uint32_t ph = (it / C::NS) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+          const uint32_t full_lead = mapa_shared(&full[s], 0);
+          uint8_t* sa = smem + C::OFF_A + s * C::A_BYTES;
+          const int kx = kb * KBB / (MODE == B_I8 ? 1 : 2);
+          if constexpr (MODE == B_W4) {
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
+            tma_load_2d_pair(sa, &tmA, full_lead, kx, row0);
+            if (!mbar_wait(&empty_b[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+            uint8_t* sq = smem + C::OFF_B + s * C::BQ_BYTES;
+            uint8_t* ssz = smem + C::OFF_SZ + s * C::SZ_BYTES;
+            const int grp = (kb * 64) / g.group_size;
+            mbar_arrive_expect_tx(&full_b[s], C::BQ_BYTES + C::SZ_BYTES);
+            tma_load_2d(sq, &tmB, &full_b[s], kb * 64, col0 / 4);
+            tma_load_2d(ssz, &tmS, &full_b[s], col0, grp);
+            tma_load_2d(ssz + HBN * 2, &tmZ, &full_b[s], col0, grp);
+          } else {
+            uint8_t* sb = smem + C::OFF_B + s * C::B_BYTES;
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES));
+            tma_load_2d_pair(sa, &tmA, full_lead, kx, row0);
+            tma_load_2d_pair(sb, &tmB, full_lead, kx, col0);
+          }
+        }
+      }
+      if (!ok) {
+        // Let loads already issued land before this CTA can exit: wait for the
+        // stage barriers this CTA can observe (its own empty barriers of the
+        // last phases -- the MMA side has aborted too -- and, in W4 mode, the
+        // local full_b barriers).
+        const uint32_t issued = it;
+        for (int s = 0; s < C::NS; ++s) {
+          const uint32_t cnt = issued > (uint32_t)s ? (issued - 1 - s) / C::NS + 1 : 0;
+          if (cnt == 0) continue;
+          if (leader) mbar_wait_drain(&full[s], (cnt - 1) & 1, 200000000ull);
+          if constexpr (MODE == B_W4) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = (MODE == B_I8) ? idesc_i8(2 * HM, PBN) : idesc_f16(2 * HM, PBN);
+      uint32_t it = 0;
+      int t_local = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t aph = (t_local >> 1) & 1;
+        if (!mbar_wait_cluster(&tmem_empty[acc], aph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMEM)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * PBN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % C::NS;
+          const uint32_t ph = (it / C::NS) & 1;
+          if (!mbar_wait_cluster(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+          const uint8_t* sb;
+          int d = 0;
+          if constexpr (MODE == B_W4) {
+            d = it % C::ND;
+            const uint32_t dph = (it / C::ND) & 1;
+            if (!mbar_wait_cluster(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+            sb = smem + C::OFF_D + d * C::B_BYTES;
+          } else {
+            sb = smem + C::OFF_B + s * C::B_BYTES;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + C::OFF_A + s * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sb);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = sdesc_sw128(a_addr + k * 32);
+            const uint64_t bd = sdesc_sw128(b_addr + k * 32);
+            if constexpr (MODE == B_I8)
+              mma_i8_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          tc_commit_pair(&empty[s], 3);
+          if constexpr (MODE == B_W4) tc_commit_pair(&empty_d[d], 3);
+        }
+        if (!ok) break;
+        tc_commit_pair(&tmem_full[acc], 3);
+      }
+      if (!ok) {
+        tc_commit(drain_bar);
+        mbar_wait_drain(drain_bar, 0, 200000000ull);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp - 4;
+    const uint32_t tmem_empty_lead0 = mapa_shared(&tmem_empty[0], 0);
+    const uint32_t tmem_empty_lead1 = mapa_shared(&tmem_empty[1], 0);
+    int t_local = 0;
+    for (int tile = cluster; tile < g.num_tiles; tile += num_clusters, ++t_local) {
+      const int m_blk = tile / g.n_blocks, n_blk = tile % g.n_blocks;
+      const int acc = t_local & 1;
+      const uint32_t aph = (t_local >> 1) & 1;
+      if (!mbar_wait_warp(&tmem_full[acc], aph, abort_flag, g.ctl, ST_TIMEOUT_TMEM)) break;
+      tc_fence_after();
+      const int row = m_blk * 2 * HM + (int)rank * HM + q * 32 + lane;
+      const uint32_t tbase = tmem_addr(tmem_base, q * 32, acc * PBN);
+      if (MODE != B_I8 && g.epi == EPI_QKV_ROPE) {
+#pragma unroll 1
+        for (int c = 0; c < PBN / 64; ++c) {
+          uint32_t r[64];
+          tmem_ld32(tbase + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld32(tbase + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_ld_wait();
+          if (row < g.M) epilogue_qkv_head(g, row, n_blk * PBN + c * 64, r);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < PBN / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+          tmem_ld_wait();
+          if (row < g.M) epilogue16<MODE>(g, row, n_blk * PBN + c * 16, r);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? tmem_empty_lead1 : tmem_empty_lead0);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dequantisation (both CTAs)
+    if constexpr (MODE == B_W4) {
+      const int dq = threadIdx.x - 256;
+      const uint32_t group = (uint32_t)(dq / HBN);   // takes the k-blocks with it % 2 == group
+      const int n = dq % HBN;           // local output channel, 0..HBN-1
+      const int grow = n >> 2;
+      const int ci = n & 3;
+      uint32_t it = 0;
+      for (int tile = cluster; tile < g.num_tiles; tile += num_clusters) {
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          if ((it & 1u) != group) continue;
+          const int s = it % C::NS;
+          const uint32_t ph = (it / C::NS) & 1;
+          if (!mbar_wait_warp(&full_b[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+          const uint8_t* sq = smem + C::OFF_B + s * C::BQ_BYTES + grow * 128;
+          const __half* ssz = reinterpret_cast<const __half*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
+          uint32_t x0[4], x1[4];
+          *reinterpret_cast<uint4*>(x0) = *reinterpret_cast<const uint4*>(sq + (((2 * ci) ^ (grow & 7)) * 16));
+          *reinterpret_cast<uint4*>(x1) = *reinterpret_cast<const uint4*>(sq + (((2 * ci + 1) ^ (grow & 7)) * 16));
+          const __half2 s2 = __half2half2(ssz[n]);
+          const __half2 z2 = __half2half2(ssz[HBN + n]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty_b[s]);
+          const int d = it % C::ND;
+          const uint32_t dph = (it / C::ND) & 1;
+          if (!mbar_wait_warp(&empty_d[d], dph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+          uint8_t* drow = smem + C::OFF_D + d * C::B_BYTES + n * 128;
+          uint4 o[4];
+          dequant_chunk(x0, s2, z2, o);
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + ((qq ^ (n & 7)) * 16)) = o[qq];
+          dequant_chunk(x1, s2, z2, o);
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(&full_d[d], 0));
+        }
+        if (!ok) break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // neither CTA frees TMEM or exits while its peer may still use the pair
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int MODE>
+int launch2(const GemmLaunch& L) {
+  using C = Cfg2<MODE>;
+  const DeviceInfo& di = device_info();
+  if (C::SMEM > di.max_smem_optin)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "gemm2sm: %d B shared memory exceeds %d", C::SMEM, di.max_smem_optin);
+  CUtensorMap tmA, tmB, tmS, tmZ;
+  int rc;
+  if constexpr (MODE == B_I8) {
+    rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.a, L.K, L.M, L.lda, 128, HM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.b, L.K, L.N, L.K, 128, HBN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    tmS = tmB;
+    tmZ = tmB;
+  } else {
+    rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.a, L.K, L.M, L.lda * 2, 64, HM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if constexpr (MODE == B_W4) {
+      rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT16, L.b, L.K, L.N / 4, L.K * 2, 64, HBN / 4,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      rc = tmap_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.scales, L.N, L.gpad, L.N * 2, HBN, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+      rc = tmap_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.zeros, L.N, L.gpad, L.N * 2, HBN, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+    } else {
+      rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.b, L.K, L.N, L.K * 2, 64, HBN, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      tmS = tmB;
+      tmZ = tmB;
+    }
+  }
+  GemmArgs g;
+  g.M = (int)L.M;
+  g.N = (int)L.N;
+  g.K = (int)L.K;
+  g.n_blocks = (int)(L.N / PBN);
+  const int m_blocks = (int)((L.M + 2 * HM - 1) / (2 * HM));
+  g.num_tiles = m_blocks * g.n_blocks;
+  g.num_kb = (int)(L.K * (MODE == B_I8 ? 1 : 2) / KBB);
+  g.group_size = L.group_size;
+  g.epi = L.epi;
+  g.bias = reinterpret_cast<const __half*>(L.bias);
+  g.out = reinterpret_cast<__half*>(L.out);
+  g.ldo = L.ldo;
+  g.resid = reinterpret_cast<const __half*>(L.resid);
+  g.ldr = L.ldr;
+  g.gamma = reinterpret_cast<const __half*>(L.gamma);
+  g.wscale = reinterpret_cast<const __half*>(L.wscale);
+  g.ascale = reinterpret_cast<const __half*>(L.ascale);
+  g.rope = L.rope;
+  g.ctl = make_ctl();
+  if (g.num_tiles == 0) return QVGGT_OK;
+
+  auto kfn = gemm2sm_kernel<MODE>;
+  static bool attr_set[64] = {};
+  if (di.device < 64 && !attr_set[di.device]) {
+    rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                    "cudaFuncSetAttribute(gemm2sm)");
+    if (rc) return rc;
+    attr_set[di.device] = true;
+  }
+  const int max_clusters = di.num_sms / 2;
+  const int clusters = g.num_tiles < max_clusters ? g.num_tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = L.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  rc = check_cuda(cudaLaunchKernelEx(&cfg, kfn, tmA, tmB, tmS, tmZ, g), "gemm2sm launch");
+  if (rc) return rc;
+  return check_cuda(cudaGetLastError(), "gemm2sm launch");
+}
+
+}  // namespace
+
+// Launches the 2-SM kernel for a shape gemm_launch has already validated;
+// requires N % 256 == 0.
+int gemm_launch_2sm(const GemmLaunch& L) {
+  switch (L.mode) {
+    case B_W4: return launch2<B_W4>(L);
+    case B_F16: return launch2<B_F16>(L);
+    case B_I8: return launch2<B_I8>(L);
+  }
+  return set_error(QVGGT_ERR_INVALID, "gemm2sm: bad mode");
+}
+
+}  // namespace qv

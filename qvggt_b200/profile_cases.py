@@ -77,12 +77,30 @@ def mem(reps=2):
     return fns
 
 
-def _time(fn, iters=20):
+def _time(fn, iters=20, graph=False):
+    """Average device time per call.  graph=True captures the `iters` calls in
+    one CUDA graph first, so host launch overhead does not pace short kernels."""
     torch.cuda.synchronize()
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
+    else:
+        def run():
+            for _ in range(iters):
+                fn()
     a, b = torch.cuda.Event(True), torch.cuda.Event(True)
     a.record()
-    for _ in range(iters):
-        fn()
+    run()
     b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / iters / 1e3
@@ -107,8 +125,13 @@ def main(argv):
             t = _time(fn)
             print(f"gemm {mode} M=43968 N=4096 K=1024: {t * 1e6:.1f} us {fl / t / 1e12:.0f} T(FL)OP/s")
         for name, (fn, nbytes) in mem().items():
-            t = _time(fn, 100)
-            print(f"{name}: {t * 1e6:.2f} us {nbytes / t / 1e9:.0f} GB/s")
+            t = _time(fn, 100, graph=True)
+            print(f"{name}: {t * 1e6:.2f} us {nbytes / t / 1e9:.0f} GB/s (CUDA-graph replay)")
+        # the BASELINE config 0 GEMV (M = 1, K = 1024, N = 4096)
+        qw, s, z = _w4(4096, 1024)
+        x1 = torch.randn(1, 1024, dtype=torch.float16, device="cuda")
+        t = _time(lambda: eng.gemv_forward_cuda_new(x1, qw, s, z, 1, 4096, 1024, 128), 200, graph=True)
+        print(f"gemv m=1 N=4096 K=1024: {t * 1e6:.2f} us {2246656 / t / 1e9:.0f} GB/s (CUDA-graph replay)")
     torch.cuda.synchronize()
     print("ok", what)
 

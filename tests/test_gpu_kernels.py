@@ -344,3 +344,41 @@ def test_qkv_rope_linear_matches_separate_path(kind, qk_norm):
     q2, kv2 = eng.qkv_rope2d(qkv, 16, cos_t, sin_t, qk_norm=qn)
     assert torch.equal(q1, q2)
     assert torch.equal(kv1, kv2)
+
+
+@pytest.mark.parametrize("mode", ["w4", "f16", "i8"])
+def test_pair_gemm_equals_single_sm_gemm(mode):
+    """With QVGGT_GEMM_2SM=1, M >= 512 runs on CTA pairs (2-SM MMA, 256-row
+    tiles) and M < 512 on the 1-SM kernel: the rows both compute must agree bit
+    for bit (same K order).  Runs in a child process (the switch is read once)."""
+    import os
+    import subprocess
+    import sys
+    if os.environ.get("QVGGT_GEMM_2SM") != "1":
+        env = dict(os.environ, QVGGT_GEMM_2SM="1")
+        r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", "-m", "gpu",
+                            f"{__file__}::test_pair_gemm_equals_single_sm_gemm[{mode}]"],
+                           env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stdout[-3000:]
+        return
+    from qvggt_b200 import awq_inference_engine as eng
+    M, N, K = 1024, 512, 1024
+    g = torch.Generator().manual_seed(31)
+    if mode == "i8":
+        a = torch.randint(-128, 128, (M, K), dtype=torch.int8, generator=g).to(DEV)
+        w = torch.randint(-128, 128, (N, K), dtype=torch.int8, generator=g).to(DEV)
+        full, part = eng.i8_gemm_i32(a, w), eng.i8_gemm_i32(a[:384].contiguous(), w)
+        assert np.array_equal(full.cpu().numpy(), ow.int8_gemm_i32(a.cpu().numpy(), w.cpu().numpy()))
+    else:
+        x = torch.randn(M, K, generator=g).half().to(DEV)
+        if mode == "w4":
+            lin, t = _lin(N, K, 128, seed=3)
+            f = lambda xx: eng.gemm_forward_cuda_new(xx, t["qweight"], t["scales"], t["scaled_zeros"])
+            ref = awq.w4a16_linear(x.cpu(), lin["qweight"], lin["scales"], lin["scaled_zeros"], 128)
+        else:
+            wt = (torch.randn(N, K, generator=g) * 0.02).half()
+            f = lambda xx: eng.f16_linear(xx, wt.to(DEV))
+            ref = om.QLinear("f16", weight=wt, bias=None)(x.cpu()).float()
+        full, part = f(x), f(x[:384].contiguous())
+        assert awq.max_abs_rel(full.cpu(), ref) <= 2e-3
+    assert torch.equal(full[:384], part)
