@@ -97,6 +97,27 @@ int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, c
                         int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
                         const void* gamma, void* stream);
 
+/* Small-M linear (1 <= M <= 256 rows; N % 128 == 0, K % 64 == 0): the same
+ * result and epilogues as qvggt_w4a16_linear_ex (weight_kind 0: AWQ int4
+ * qweight/scales/scaled_zeros/gpad/group_size) or qvggt_f16_linear_ex
+ * (weight_kind 1: fp16 weight [N, K] in `weight`, scales ignored), computed
+ * with the rows as the tensor-core N dimension and K split across the CTAs
+ * of a thread-block cluster (partials summed on chip in a fixed order; no
+ * workspace).  Replaces the small-M path of gemm_forward_cuda_new,
+ * gemm_w4a16_T1 with its split-K semaphore
+ * (E/quantization_new/gemm/gemm_cuda.cu:312-751, 1154-1205). */
+int qvggt_small_linear(int32_t weight_kind, const void* in_feats, int64_t lda, const void* weight, const void* scales,
+                       const void* scaled_zeros, int64_t gpad, int32_t group_size, const void* bias, void* out,
+                       int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
+                       const void* gamma, void* stream);
+
+/* Launch plan qvggt_small_linear uses for (M, N, K) on the current device:
+ * info[0] padded rows (MMA N), info[1] CTAs per cluster (K splits),
+ * info[2] 64-wide k-blocks per CTA, info[3] CTAs, info[4] clusters of that
+ * size the device holds at once.  Part of the same small-M replacement
+ * (E/quantization_new/gemm/gemm_cuda.cu:1154-1205 picks its tiles by M). */
+int qvggt_small_linear_plan(int32_t weight_kind, int64_t M, int64_t N, int64_t K, int32_t* info);
+
 /* out[m, N] = in_feats[m, K] . deq(qweight)^T (+ bias) for 1 <= m <= 16.
  * Any group_size that is a multiple of 32 and divides K.
  * Replaces gemv_forward_cuda_new (E/quantization_new/gemv/gemv_cuda.cu:197-281,

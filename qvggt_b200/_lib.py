@@ -30,6 +30,8 @@ SIGNATURES = {
     "qvggt_qkv_rope_linear": [vp, i32, vp, vp, vp, i64, i32, vp, vp, vp, i64, i64, i32, i64, i32, i32, i32, vp, vp,
                               i32, i32, vp, vp, vp, vp, f32, vp],
     "qvggt_w4a16_gemv": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
+    "qvggt_small_linear": [i32, vp, i64, vp, vp, vp, i64, i32, vp, vp, i64, i64, i64, i64, i32, vp, i64, vp, vp],
+    "qvggt_small_linear_plan": [i32, i64, i64, i64, C.POINTER(i32)],
     "qvggt_w8a8_gemm": [vp, vp, vp, vp, vp, vp, i64, i64, i64, vp],
     "qvggt_i8_gemm_i32": [vp, vp, vp, i64, i64, i64, vp],
     "qvggt_w8a8_gemm_residual": [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp],

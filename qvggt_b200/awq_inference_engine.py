@@ -25,7 +25,7 @@ __all__ = [
     "gemm_forward_cuda_new", "gemv_forward_cuda_new", "w8a8_gemm_forward_cuda",
     "w8a8_gemm_fuse_bias_forward_cuda", "invoke_quant", "rms_norm_general", "gelu_and_quant",
     "fused_rope_with_pos_forward_func", "w4a16_linear", "f16_linear", "layernorm", "qkv_rope2d",
-    "attention", "i8_gemm_i32",
+    "attention", "i8_gemm_i32", "small_linear",
 ]
 
 
@@ -95,8 +95,11 @@ def gemm_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, group_size: i
     M = in_feats.numel() // K
     out = torch.empty(*in_feats.shape[:-1], N, dtype=in_feats.dtype, device=dev)
     with _Dev(dev):
-        _lib.call("qvggt_w4a16_gemm", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
-                  _ptr(out), M, N, K, scales.shape[0], group_size, _stream(in_feats))
+        if 1 <= M <= SMALL_M_MAX:
+            _small_linear(0, in_feats, qweight, scales, scaled_zeros, group_size, None, out, M, N, K, 0, None, None)
+        else:
+            _lib.call("qvggt_w4a16_gemm", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
+                      _ptr(out), M, N, K, scales.shape[0], group_size, _stream(in_feats))
     return out
 
 
@@ -123,8 +126,10 @@ def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 
                  residual=None, gamma=None, out=None):
     """Fused W4A16 linear: ``half(half(x.W^T) + bias)`` then optionally
     ``gelu`` (act='gelu') or an in-place LayerScale residual update
-    ``residual += half(y * gamma)`` (returns ``residual``).  m <= 16 rows use
-    the GEMV kernel (plain / bias epilogue only)."""
+    ``residual += half(y * gamma)`` (returns ``residual``).  Up to
+    ``GEMV_M_MAX`` rows (plain / bias epilogue) use the GEMV kernel, up to
+    ``SMALL_M_MAX`` rows the split-K small-M kernel, more the persistent
+    tcgen05 GEMM."""
     name = "w4a16_linear"
     dev = _check_cuda(name, x, qweight, scales, scaled_zeros, bias, residual, gamma)
     _contig(name, x, qweight, scales, scaled_zeros, bias, gamma)
@@ -136,9 +141,12 @@ def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 
     elif out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
     with _Dev(dev):
-        if M <= 16 and act is None and residual is None:
+        if M <= GEMV_M_MAX and act is None and residual is None:
             _lib.call("qvggt_w4a16_gemv", _ptr(x), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), _ptr(bias),
                       _ptr(out), M, N, K, scales.shape[0], group_size, _stream(x))
+        elif 1 <= M <= SMALL_M_MAX:
+            _small_linear(0, x, qweight, scales, scaled_zeros, group_size, bias, out, M, N, K,
+                          1 if act == "gelu" else 0, residual, gamma)
         else:
             _lib.call("qvggt_w4a16_linear_ex", _ptr(x), K, _ptr(qweight), _ptr(scales), _ptr(scaled_zeros),
                       _ptr(bias), _ptr(out), N, M, N, K, scales.shape[0], group_size, 1 if act == "gelu" else 0,
@@ -188,9 +196,57 @@ def f16_linear(x, weight, bias=None, act: str | None = None, residual=None, gamm
     elif out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
     with _Dev(dev):
-        _lib.call("qvggt_f16_linear_ex", _ptr(x), K, _ptr(weight), _ptr(bias), _ptr(out), N, M, N, K,
-                  1 if act == "gelu" else 0, _ptr(residual), N if residual is not None else 0, _ptr(gamma),
-                  _stream(x))
+        if 1 <= M <= SMALL_M_MAX:
+            _small_linear(1, x, weight, None, None, 128, bias, out, M, N, K, 1 if act == "gelu" else 0,
+                          residual, gamma)
+        else:
+            _lib.call("qvggt_f16_linear_ex", _ptr(x), K, _ptr(weight), _ptr(bias), _ptr(out), N, M, N, K,
+                      1 if act == "gelu" else 0, _ptr(residual), N if residual is not None else 0, _ptr(gamma),
+                      _stream(x))
+    return out
+
+
+# ------------------------------------------------------------------- small M
+# Row counts routed to the split-K small-M kernel (qvggt_small_linear); up to
+# GEMV_M_MAX rows without a fused activation/residual use the GEMV.  Measured
+# on B200 at the camera-trunk shapes (dim 2048, one row per frame).
+SMALL_M_MAX = 256
+GEMV_M_MAX = 4
+
+
+def _small_linear(kind, x, w, scales, zeros, group_size, bias, out, M, N, K, act, residual, gamma):
+    _lib.call("qvggt_small_linear", kind, _ptr(x), K, _ptr(w), _ptr(scales), _ptr(zeros),
+              scales.shape[0] if scales is not None else 0, group_size, _ptr(bias), _ptr(out), N, M, N, K, act,
+              _ptr(residual), N if residual is not None else 0, _ptr(gamma), _stream(x))
+
+
+def small_linear_plan(weight_kind: int, M: int, N: int, K: int) -> dict:
+    """Launch plan of :func:`small_linear` on the current device."""
+    info = (C.c_int32 * 5)()
+    _lib.call("qvggt_small_linear_plan", weight_kind, M, N, K, info)
+    return dict(rows=info[0], splits=info[1], kb_per_cta=info[2], ctas=info[3], active_clusters=info[4])
+
+
+def small_linear(x, weight, scales=None, scaled_zeros=None, bias=None, group_size: int = 128,
+                 act: str | None = None, residual=None, gamma=None, out=None):
+    """Linear for 1..256 rows on the split-K small-M kernel (always, whatever
+    ``SMALL_M_MAX`` says): W4A16 when
+    ``scales`` is given (``weight`` = qweight int16 [N/4, K]), else dense fp16
+    ``weight`` [N, K].  Same epilogues and rounding as :func:`w4a16_linear`."""
+    name = "small_linear"
+    dev = _check_cuda(name, x, weight, scales, scaled_zeros, bias, residual, gamma)
+    _contig(name, x, weight, scales, scaled_zeros, bias, gamma)
+    kind = 0 if scales is not None else 1
+    K = x.shape[-1]
+    N = weight.shape[0] * (4 if kind == 0 else 1)
+    M = x.numel() // K
+    if residual is not None:
+        out = residual
+    elif out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
+    with _Dev(dev):
+        _small_linear(kind, x, weight, scales, scaled_zeros, group_size, bias, out, M, N, K,
+                      1 if act == "gelu" else 0, residual, gamma)
     return out
 
 

@@ -232,6 +232,41 @@ int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, c
   return rc;
 }
 
+int qvggt_small_linear_plan(int32_t weight_kind, int64_t M, int64_t N, int64_t K, int32_t* info) {
+  if (!info) return set_error(QVGGT_ERR_INVALID, "small_linear_plan: info is null");
+  if (weight_kind != 0 && weight_kind != 1) return set_error(QVGGT_ERR_INVALID, "small_linear: weight_kind");
+  SmallPlan P;
+  int rc = gemm_small_plan(weight_kind == 0 ? B_W4 : B_F16, M, N, K, 0, &P);
+  if (rc) return rc;
+  info[0] = P.mt;
+  info[1] = P.splits;
+  info[2] = P.kb_per_split;
+  info[3] = P.n_blocks * P.splits;
+  info[4] = P.active_clusters;
+  return QVGGT_OK;
+}
+
+int qvggt_small_linear(int32_t weight_kind, const void* in_feats, int64_t lda, const void* weight, const void* scales,
+                       const void* scaled_zeros, int64_t gpad, int32_t group_size, const void* bias, void* out,
+                       int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
+                       const void* gamma, void* stream) {
+  if (weight_kind != 0 && weight_kind != 1) return set_error(QVGGT_ERR_INVALID, "small_linear: weight_kind");
+  if (resid && act) return set_error(QVGGT_ERR_INVALID, "act and residual are exclusive");
+  if (resid && resid != out) return set_error(QVGGT_ERR_INVALID, "residual epilogue updates in place: out == resid");
+  SmallPlan P;
+  int rc = gemm_small_plan(weight_kind == 0 ? B_W4 : B_F16, M, N, K, 0, &P);
+  if (rc) return rc;
+  GemmLaunch L;
+  L.mode = weight_kind == 0 ? B_W4 : B_F16;
+  L.epi = resid ? EPI_RESID : (act == 1 ? EPI_GELU : EPI_STORE);
+  L.a = in_feats; L.lda = lda; L.b = weight; L.scales = scales; L.zeros = scaled_zeros; L.gpad = gpad;
+  L.group_size = group_size; L.bias = bias; L.out = out; L.ldo = ldo; L.resid = resid; L.ldr = ldr;
+  L.gamma = gamma; L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  rc = gemm_small_launch(L, P);
+  if (rc == QVGGT_OK) count_launch(1);
+  return rc;
+}
+
 int qvggt_w8a8_gemm(const int8_t* in, const int8_t* w, const void* wscales, const void* ascales, const void* bias,
                     void* out, int64_t M, int64_t N, int64_t K, void* stream) {
   GemmLaunch L;

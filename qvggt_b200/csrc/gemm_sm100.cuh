@@ -56,4 +56,20 @@ int gemm_launch(const GemmLaunch& L);
 // 2-SM (CTA-pair) variant for large M; called by gemm_launch after validation.
 int gemm_launch_2sm(const GemmLaunch& L);
 
+// Small-M split-K GEMM on thread-block clusters (gemm_small.cu): 1 <= M <= 256,
+// modes B_W4 / B_F16, epilogues EPI_STORE / EPI_GELU / EPI_RESID.
+struct SmallPlan {
+  int mt = 16;              // padded row count (the MMA's N)
+  int n_blocks = 0;         // 128-channel tiles
+  int num_kb = 0;           // 64-wide k-blocks
+  int splits = 1;           // K ranges per channel tile = CTAs per cluster (<= 8)
+  int kb_per_split = 0;
+  int smem = 0;
+  int active_clusters = 0;  // co-resident clusters of `splits` CTAs (occupancy query)
+};
+// Chooses the tile height and K split for the current device; max_splits > 0
+// caps the split count.
+int gemm_small_plan(int mode, long long M, long long N, long long K, int max_splits, SmallPlan* P);
+int gemm_small_launch(const GemmLaunch& L, const SmallPlan& P);
+
 }  // namespace qv

@@ -3,6 +3,8 @@
     python -m qvggt_b200.profile_cases attn  [L] [batches]   # flash attention, 16 heads x 64
     python -m qvggt_b200.profile_cases gemm  f16|w4|w8 [M]    # tcgen05 GEMM, N=4096 K=1024
     python -m qvggt_b200.profile_cases mem                    # LayerNorm, invoke_quant, GEMV
+    python -m qvggt_b200.profile_cases small [M] [N] [K]      # small-M split-K GEMM (camera trunk)
+    python -m qvggt_b200.profile_cases small_time             # small-M vs large kernel vs GEMV
     python -m qvggt_b200.profile_cases time                   # CUDA-event timings of all of the above
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
@@ -77,6 +79,63 @@ def mem(reps=2):
     return fns
 
 
+def small(M=32, N=6144, K=2048, reps=2):
+    qw, s, z = _w4(N, K)
+    x = torch.randn(M, K, dtype=torch.float16, device="cuda")
+    out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    fn = lambda: eng.small_linear(x, qw, s, z, out=out)
+    for _ in range(reps):
+        fn()
+    return fn
+
+
+def _rotating(N, K, total=256 << 20):
+    """Enough copies of a W4 weight that cycling through them streams > L2."""
+    wbytes = N * K // 2 + 2 * (K // 128) * N * 2
+    return [_w4(N, K, seed=i) for i in range(max(2, -(-total // wbytes)))]
+
+
+def small_time():
+    """Camera-trunk linears (dim 2048) at M = 1..256 rows: the split-K small-M
+    kernel, the large tcgen05 kernel and (M <= 16) the GEMV, each cycling
+    through weight copies larger than L2 (HBM-bound), CUDA-graph replay."""
+    for N, K in ((6144, 2048), (2048, 2048), (8192, 2048), (2048, 8192)):
+        ws = _rotating(N, K)
+        wbytes = N * K // 2 + 2 * (K // 128) * N * 2
+        for M in (1, 8, 16, 32, 64, 128, 192, 256):
+            x = torch.randn(M, K, dtype=torch.float16, device="cuda")
+            out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+            nbytes = wbytes + M * K * 2 + M * N * 2
+            it = [0]
+
+            def nxt():
+                w = ws[it[0] % len(ws)]
+                it[0] += 1
+                return w
+
+            def f_small():
+                qw, s, z = nxt()
+                eng.small_linear(x, qw, s, z, out=out)
+
+            def f_large():
+                qw, s, z = nxt()
+                _lib.call("qvggt_w4a16_linear_ex", x.data_ptr(), K, qw.data_ptr(), s.data_ptr(), z.data_ptr(), None,
+                          out.data_ptr(), N, M, N, K, s.shape[0], 128, 0, None, 0, None,
+                          torch.cuda.current_stream().cuda_stream)
+
+            def f_gemv():
+                qw, s, z = nxt()
+                eng.gemv_forward_cuda_new(x, qw, s, z, M, N, K, 128)
+
+            pl = eng.small_linear_plan(0, M, N, K)
+            row = [f"N={N} K={K} M={M} [splits {pl['splits']} ctas {pl['ctas']} active {pl['active_clusters']}]:"]
+            cases = [("small", f_small), ("large", f_large)] + ([("gemv", f_gemv)] if M <= 16 else [])
+            for name, f in cases:
+                t = _time(f, len(ws), graph=True)
+                row.append(f"{name} {t * 1e6:.2f} us ({nbytes / t / 1e9:.0f} GB/s)")
+            print("  ".join(row))
+
+
 def _time(fn, iters=20, graph=False):
     """Average device time per call.  graph=True captures the `iters` calls in
     one CUDA graph first, so host launch overhead does not pace short kernels."""
@@ -115,6 +174,10 @@ def main(argv):
         gemm(argv[1] if len(argv) > 1 else "f16", *(int(v) for v in argv[2:3]))
     elif what == "mem":
         mem()
+    elif what == "small":
+        small(*(int(v) for v in argv[1:4]))
+    elif what == "small_time":
+        small_time()
     elif what == "time":
         for L, b in ((16384, 1), (43968, 1), (1374, 32)):
             fn, fl = attn(L, b)

@@ -117,7 +117,8 @@ class WQLinear(nn.Module):
 
     @torch.no_grad()
     def forward(self, x):
-        """y = x . deq(W)^T + bias: GEMV for up to 16 rows, tcgen05 GEMM otherwise."""
+        """y = x . deq(W)^T + bias: GEMV for a few rows, the split-K small-M
+        tcgen05 kernel up to 256 rows, the persistent tcgen05 GEMM beyond."""
         return engine.w4a16_linear(x.contiguous(), self.qweight, self.scales, self.scaled_zeros, self.bias,
                                    self.group_size)
 
