@@ -11,15 +11,20 @@
 // Schedule: a softmax warpgroup releases S_i (s_free) as soon as its TMEM read
 // of the row completes, so the tensor core computes S_i(j+1) while the
 // warpgroup is still exponentiating tile j; P_i is written only after
-// PV_i(j-1) has finished reading the previous P_i (o_done).
+// PV_i(j-1) has finished reading the previous P_i (o_done).  K and V stages
+// are released separately: a K stage as soon as both S MMAs that read it
+// complete, a V stage after both PV MMAs, and K and V have their own producer
+// threads, so the K tiles for S(j+1..j+3) stream in while PV(j) still waits
+// for the softmax of tile j.
 // The running maximum m is only raised when a row's new maximum exceeds it by
 // more than 2^8 (then O_i and the row sum are rescaled in place); P <= 256 fits
 // fp16 and the final O / l is exact either way.
 //
 // TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 //               O0 [384,448) O1 [448,512).
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 4..7 softmax WG 0,
-// 8..11 softmax WG 1.  All waits are bounded (common.cuh).
+// Warps: 0 TMA producer of Q and K, 2 TMA producer of V, 1 TMEM owner + MMA
+// issuer, 4..7 softmax WG 0, 8..11 softmax WG 1.  All waits are bounded
+// (common.cuh).
 #include <cstdlib>
 
 #include "host.hpp"
@@ -40,8 +45,9 @@ struct AttnSmem {
   static constexpr int K = Q1 + TILE_BYTES;
   static constexpr int V = K + KV_STAGES * TILE_BYTES;
   static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
-  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], o_done[2], drain
-  static constexpr int NUM_BARS = 1 + 3 * KV_STAGES + 8 + 1;
+  // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], s_free[2], p_full[2],
+  // o_done[2], drain
+  static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 1;
   static constexpr int MISC = BAR + NUM_BARS * 8;
   static constexpr int TOTAL = MISC + 16 + 1024;
 };
@@ -122,16 +128,14 @@ __device__ __forceinline__ void exp2_poly_pair(uint64_t x2, float& p0, float& p1
   p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
-// p = exp2(s*c - m) (0 beyond `valid`), accumulated into l, packed as fp16
-// pairs into s[0..63] (in place: pair e is read before slot e is written).
-// POLY of every 8 pairs use the FMA-pipe polynomial, the rest MUFU ex2, which
-// balances the two pipes (MUFU issues 16 results per SM per clock).
-template <bool PARTIAL, int POLY>
-__device__ __forceinline__ float exp_pack(uint32_t (&s)[128], float c, float neg_m, int valid) {
-  const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
-  uint64_t l2 = f2_pack(0.f, 0.f);
+// Pairs E0..E0+15 of p = exp2(s*c - m) (0 beyond `valid`), added into l2 and
+// packed as fp16 pairs into s[E0..E0+15] (in place: chunk E0/16 reads scores
+// s[2*E0..2*E0+31], which no earlier chunk wrote).  POLY of every 8 pairs use
+// the FMA-pipe polynomial, the rest MUFU ex2 (16 results per SM per clock).
+template <bool PARTIAL, int POLY, int E0>
+__device__ __forceinline__ void exp_chunk(uint32_t (&s)[128], uint64_t c2, uint64_t nm2, uint64_t& l2, int valid) {
 #pragma unroll
-  for (int e = 0; e < 64; ++e) {
+  for (int e = E0; e < E0 + 16; ++e) {
     const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), c2, nm2);
     float p0, p1;
     if ((e & 7) < POLY) {
@@ -149,6 +153,33 @@ __device__ __forceinline__ float exp_pack(uint32_t (&s)[128], float c, float neg
     l2 = f2_add(l2, f2_pack(p0, p1));
     s[e] = pack_half2(p0, p1);
   }
+}
+
+// P = exp2(S*c - m) for the thread's row, written to TMEM in four 16-column
+// chunks as they are produced: each tcgen05.st is asynchronous until the one
+// wait at the end, so three of the four stores overlap the exponentials still
+// to come.  P may be written only once PV(j-1) has read the previous P: that
+// wait (`o_ready` false) comes just before the first store.  Returns the row
+// sum of P, or NaN if the wait gave up.
+template <bool PARTIAL, int POLY>
+__device__ __forceinline__ float exp_store(uint32_t (&s)[128], float c, float neg_m, int valid, uint32_t tP,
+                                           bool o_ready, uint64_t* o_done, uint32_t o_parity,
+                                           volatile int* abort_flag, const Ctl& ctl) {
+  const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
+  uint64_t l2 = f2_pack(0.f, 0.f);
+  exp_chunk<PARTIAL, POLY, 0>(s, c2, nm2, l2, valid);
+  if (!o_ready) {
+    if (!mbar_wait_warp(o_done, o_parity, abort_flag, ctl, ST_TIMEOUT_SOFTMAX)) return __int_as_float(0x7fc00000);
+    tc_fence_after();
+  }
+  tmem_st16(tP + 0, *reinterpret_cast<const uint32_t(*)[16]>(&s[0]));
+  exp_chunk<PARTIAL, POLY, 16>(s, c2, nm2, l2, valid);
+  tmem_st16(tP + 16, *reinterpret_cast<const uint32_t(*)[16]>(&s[16]));
+  exp_chunk<PARTIAL, POLY, 32>(s, c2, nm2, l2, valid);
+  tmem_st16(tP + 32, *reinterpret_cast<const uint32_t(*)[16]>(&s[32]));
+  exp_chunk<PARTIAL, POLY, 48>(s, c2, nm2, l2, valid);
+  tmem_st16(tP + 48, *reinterpret_cast<const uint32_t(*)[16]>(&s[48]));
+  tmem_st_wait();
   float l0, l1;
   f2_unpack(l2, l0, l1);
   return l0 + l1;
@@ -164,8 +195,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + KV_STAGES;
-  uint64_t* kv_empty = v_full + KV_STAGES;
-  uint64_t* s_full = kv_empty + KV_STAGES;  // [2] MMA -> softmax: S_i ready
+  uint64_t* k_empty = v_full + KV_STAGES;   // [S] MMA -> K producer: S_0, S_1 of the tile done
+  uint64_t* v_empty = k_empty + KV_STAGES;  // [S] MMA -> V producer: PV_0, PV_1 of the tile done
+  uint64_t* s_full = v_empty + KV_STAGES;   // [2] MMA -> softmax: S_i ready
   uint64_t* s_free = s_full + 2;            // [2] softmax -> MMA: S_i read
   uint64_t* p_full = s_free + 2;            // [2] softmax -> MMA: P_i written
   uint64_t* o_done = p_full + 2;            // [2] MMA -> softmax: PV_i complete
@@ -186,7 +218,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -217,31 +250,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   // warpgroups take 216 each: 128*56 + 256*216 = 62464 <= 64512.
   if (warp < 4) {
     regs_dec<56>();
-    if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ TMA producers (K + Q / V)
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-      tma_load_3d(smem + AttnSmem::Q0, &tmQ, q_full, 0, h, (int)q_row0);
-      tma_load_3d(smem + AttnSmem::Q1, &tmQ, q_full, 0, h, (int)(q_row0 + 128));
+      const bool is_k = warp == 0;
+      const CUtensorMap* tm = is_k ? &tmK : &tmV;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* base = smem + (is_k ? AttnSmem::K : AttnSmem::V);
+      if (is_k) {
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+        tma_load_3d(smem + AttnSmem::Q0, &tmQ, q_full, 0, h, (int)q_row0);
+        tma_load_3d(smem + AttnSmem::Q1, &tmQ, q_full, 0, h, (int)(q_row0 + 128));
+      }
       int j = 0;
       for (; j < nkv; ++j) {
         const int st = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, a.ctl, ST_TIMEOUT_TMA_EMPTY)) break;
+        if (!mbar_wait(&empty[st], ph ^ 1, abort_flag, a.ctl, ST_TIMEOUT_TMA_EMPTY)) break;
         const int row = (int)(kv_row0 + (long long)j * 128);
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(smem + AttnSmem::K + st * TILE_BYTES, &tmK, &k_full[st], 0, h, row);
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(smem + AttnSmem::V + st * TILE_BYTES, &tmV, &v_full[st], 0, h, row);
+        mbar_arrive_expect_tx(&full[st], TILE_BYTES);
+        tma_load_3d(base + st * TILE_BYTES, tm, &full[st], 0, h, row);
       }
       if (j < nkv) {
         // aborted: let the loads already issued land before the CTA exits
-        mbar_wait_drain(q_full, 0, 200000000ull);
-        for (int jj = (j > KV_STAGES ? j - KV_STAGES : 0); jj < j; ++jj) {
-          const int st = jj % KV_STAGES;
-          mbar_wait_drain(&k_full[st], (jj / KV_STAGES) & 1, 200000000ull);
-          mbar_wait_drain(&v_full[st], (jj / KV_STAGES) & 1, 200000000ull);
-        }
+        if (is_k) mbar_wait_drain(q_full, 0, 200000000ull);
+        for (int jj = (j > KV_STAGES ? j - KV_STAGES : 0); jj < j; ++jj)
+          mbar_wait_drain(&full[jj % KV_STAGES], (jj / KV_STAGES) & 1, 200000000ull);
       }
     }
   } else if (warp == 1) {
@@ -270,7 +305,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           issue_pv(i, jj);
         }
-        tc_commit(&kv_empty[jj % KV_STAGES]);
+        tc_commit(&v_empty[jj % KV_STAGES]);
         return true;
       };
       for (int j = 0; ok && j < nkv; ++j) {
@@ -289,6 +324,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                        idesc_s, k > 0 ? 1u : 0u);
           tc_commit(&s_full[i]);
         }
+        if (ok) tc_commit(&k_empty[st]);
         if (ok && j > 0) ok = pv_pair(j - 1);
       }
       if (ok && nkv > 0) ok = pv_pair(nkv - 1);
@@ -347,17 +383,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         l *= alpha;
         m_used = m_target;
       }
-      l += (valid == 128) ? exp_pack<false, POLY>(s, c, -m_used, valid) : exp_pack<true, POLY>(s, c, -m_used, valid);
-      // P_i may be overwritten only once PV_i(j-1) has read it
-      if (!o_ready) {
-        if (!mbar_wait_warp(&o_done[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
-        tc_fence_after();
-      }
-      tmem_st16(tP + 0, *reinterpret_cast<const uint32_t(*)[16]>(&s[0]));
-      tmem_st16(tP + 16, *reinterpret_cast<const uint32_t(*)[16]>(&s[16]));
-      tmem_st16(tP + 32, *reinterpret_cast<const uint32_t(*)[16]>(&s[32]));
-      tmem_st16(tP + 48, *reinterpret_cast<const uint32_t(*)[16]>(&s[48]));
-      tmem_st_wait();
+      const uint32_t o_par = (uint32_t)(j - 1) & 1;
+      const float lj = (valid == 128)
+          ? exp_store<false, POLY>(s, c, -m_used, valid, tP, o_ready, &o_done[i], o_par, abort_flag, a.ctl)
+          : exp_store<true, POLY>(s, c, -m_used, valid, tP, o_ready, &o_done[i], o_par, abort_flag, a.ctl);
+      if (__any_sync(0xffffffffu, lj != lj)) { ok = false; break; }
+      l += lj;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[i]);
@@ -451,8 +482,10 @@ extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, 
   a.ctl = make_ctl();
   const long long grid = (long long)a.nqb * heads * batches;
   if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
-  // Share of exponentials computed on the FMA pipe (pairs per 8); the
-  // QVGGT_ATTN_POLY environment variable (0..4) overrides the default.
+  // Share of exponentials computed on the FMA pipe (pairs per 8).  Measured
+  // on B200 with the chunked P stores: 0 is fastest (757 TFLOP/s at L=16384
+  // vs 713-723 for 1-2); the QVGGT_ATTN_POLY environment variable (0..4)
+  // overrides the default.
   static int poly = -1;
   if (poly < 0) {
     const char* e = getenv("QVGGT_ATTN_POLY");
