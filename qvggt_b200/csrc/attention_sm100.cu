@@ -134,6 +134,8 @@ __device__ __forceinline__ void exp2_poly_pair(uint64_t x2, float& p0, float& p1
 // the FMA-pipe polynomial, the rest MUFU ex2 (16 results per SM per clock).
 template <bool PARTIAL, int POLY, int E0>
 __device__ __forceinline__ void exp_chunk(uint32_t (&s)[128], uint64_t c2, uint64_t nm2, uint64_t& l2, int valid) {
+  // two partial sums (even / odd pairs) keep the add chain short
+  uint64_t la = f2_pack(0.f, 0.f), lb = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int e = E0; e < E0 + 16; ++e) {
     const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), c2, nm2);
@@ -150,9 +152,11 @@ __device__ __forceinline__ void exp_chunk(uint32_t (&s)[128], uint64_t c2, uint6
       if (2 * e >= valid) p0 = 0.f;
       if (2 * e + 1 >= valid) p1 = 0.f;
     }
-    l2 = f2_add(l2, f2_pack(p0, p1));
+    if (e & 1) lb = f2_add(lb, f2_pack(p0, p1));
+    else la = f2_add(la, f2_pack(p0, p1));
     s[e] = pack_half2(p0, p1);
   }
+  l2 = f2_add(l2, f2_add(la, lb));
 }
 
 // P = exp2(S*c - m) for the thread's row, written to TMEM in four 16-column
