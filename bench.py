@@ -38,6 +38,15 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# DRAM traffic of the global-attention kernel, from one ncu capture of the same
+# kernel at Lq = Lkv = 16384, 16 heads (`python -m qvggt_b200.profile_cases attn
+# 16384 1`): dram__bytes_read.sum = 100.835 MB (Q, K, V once each; K/V re-reads
+# by the 64 CTAs of a head hit L2), dram__bytes_write.sum = 17.091 MB (O; the
+# rest of O is still in L2 when the kernel ends).  Q and O scale with Lq, K and
+# V with Lkv, so a launch moves READ/3 * (Lq + 2 Lkv) + WRITE * Lq bytes.
+ATTN_READ_PER_ROW = 100.835072e6 / 16384
+ATTN_WRITE_PER_ROW = 17.091328e6 / 16384
+
 METRIC = "frames/sec VGGT-1B W4A16 forward @ S frames"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -274,6 +283,8 @@ def main():
         v, cores, sample = cpu_oracle_sample(S)
         cpu = {"value": v, "unit": "frames/s", "cores": cores, "kind": "port", "sample": sample}
 
+    Lq = S_local * cfg.tokens_per_frame
+    Lkv = S * cfg.tokens_per_frame
     if rank == 0:
         clocks = clk.summary()
         line = {
@@ -290,7 +301,9 @@ def main():
                     "d2h_bytes_per_step": out_host.numel() * 2 * ws},
             "roofline": {"kernel": "flash attention (global block)", "bound": "tensor",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": (achieved / peak) if achieved else None, "traffic": None,
+                         "frac": (achieved / peak) if achieved else None,
+                         "traffic": ATTN_READ_PER_ROW / 3 * (Lq + 2 * Lkv) + ATTN_WRITE_PER_ROW * Lq,
+                         "traffic_source": "ncu dram bytes of the same kernel at L=16384, scaled by rows",
                          "peak_source": f"{peak_kind} bf16 dense sustained",
                          "launches_timed": len(attn_ms), "avg_launch_ms": avg_attn * 1000.0,
                          "flop_per_launch": attn_flop},
