@@ -22,8 +22,8 @@
 //
 // TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 //               O0 [384,448) O1 [448,512).
-// Warps: 0 TMA producer of Q and K, 2 TMA producer of V, 1 TMEM owner + MMA
-// issuer, 4..7 softmax WG 0, 8..11 softmax WG 1.  All waits are bounded
+// Warps: 0 TMA producer of Q and K, 2 TMA producer of V, 1 TMEM owner + S
+// MMA issuer, 3 PV MMA issuer, 4..7 softmax WG 0, 8..11 softmax WG 1.  All waits are bounded
 // (common.cuh).
 #include <cstdlib>
 
@@ -46,8 +46,8 @@ struct AttnSmem {
   static constexpr int V = K + KV_STAGES * TILE_BYTES;
   static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
   // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], s_free[2], p_full[2],
-  // o_done[2], drain
-  static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 1;
+  // o_done[2], drain (S issuer), drain2 (PV issuer)
+  static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 2;
   static constexpr int MISC = BAR + NUM_BARS * 8;
   static constexpr int TOTAL = MISC + 16 + 1024;
 };
@@ -67,6 +67,15 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// tcgen05.ld writes its destination registers asynchronously: they are valid
+// only after tcgen05.wait::ld.  This empty asm takes s[A..B) as in-out
+// operands after the wait, so the compiler cannot move reads of them above it.
+template <int A, int B>
+__device__ __forceinline__ void reg_fence(uint32_t (&s)[128]) {
+#pragma unroll
+  for (int k = A; k < B; ++k) asm volatile("" : "+r"(s[k]));
+}
+
 // Loads the thread's 128 S values (4 x 32 columns) with one wait.
 __device__ __forceinline__ void load_s_row(uint32_t tS, uint32_t (&s)[128]) {
   tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
@@ -74,6 +83,7 @@ __device__ __forceinline__ void load_s_row(uint32_t tS, uint32_t (&s)[128]) {
   tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
   tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
   tmem_ld_wait();
+  reg_fence<0, 128>(s);
 }
 
 template <bool PARTIAL>
@@ -206,6 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* p_full = s_free + 2;            // [2] softmax -> MMA: P_i written
   uint64_t* o_done = p_full + 2;            // [2] MMA -> softmax: PV_i complete
   uint64_t* drain = o_done + 2;
+  uint64_t* drain2 = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AttnSmem::MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + AttnSmem::MISC + 4);
 
@@ -232,6 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(drain2, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -252,6 +264,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // Registers: launched at 168 per thread (384 x 168 = 64512); warpgroup 0
   // (producer, MMA, two idle warps) gives back to 56, the two softmax
   // warpgroups take 216 each: 128*56 + 256*216 = 62464 <= 64512.
+  // setmaxnreg is warpgroup-collective: all four warps of a warpgroup must
+  // execute the same one (a warpgroup whose warps disagree never completes
+  // it, and the other warpgroups' increments then wait forever).
   if (warp < 4) {
     regs_dec<56>();
     if (warp == 0 || warp == 2) {
@@ -284,34 +299,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ S = Q K^T issuer
+    // S and PV MMAs are issued by two threads (warps 1 and 3): each
+    // tcgen05.mma costs its issuing thread tens of cycles, so with one issuer
+    // the next tile's S had to queue behind both PVs of the previous tile.
+    // Each thread commits (and, on abort, drains) only its own MMAs.
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, 128);
-      constexpr uint32_t idesc_o = idesc_f16(128, 64, false, true);   // B = V, MN-major
       const uint32_t q_addr[2] = {smem_u32(smem + AttnSmem::Q0), smem_u32(smem + AttnSmem::Q1)};
       bool ok = mbar_wait(q_full, 0, abort_flag, a.ctl, ST_TIMEOUT_FULL);
-      auto issue_pv = [&](int i, int jj) {
-        const int st = jj % KV_STAGES;
-        const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_f16_ts(tmem + COL_O0 + i * 64, tmem + COL_P0 + i * 64 + k * 8, sdesc_sw128(v_addr + k * 2048), idesc_o,
-                     (jj > 0 || k > 0) ? 1u : 0u);
-        tc_commit(&o_done[i]);
-      };
-      // PV_0(jj), PV_1(jj), then release K/V stage of tile jj.
-      auto pv_pair = [&](int jj) -> bool {
-        for (int i = 0; i < 2; ++i) {
-          if (!mbar_wait(&p_full[i], jj & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) return false;
-          if (i == 0 && !mbar_wait(&v_full[jj % KV_STAGES], (jj / KV_STAGES) & 1, abort_flag, a.ctl,
-                                   ST_TIMEOUT_FULL))
-            return false;
-          tc_fence_after();
-          issue_pv(i, jj);
-        }
-        tc_commit(&v_empty[jj % KV_STAGES]);
-        return true;
-      };
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % KV_STAGES;
         if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
@@ -329,12 +325,38 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_commit(&s_full[i]);
         }
         if (ok) tc_commit(&k_empty[st]);
-        if (ok && j > 0) ok = pv_pair(j - 1);
       }
-      if (ok && nkv > 0) ok = pv_pair(nkv - 1);
       if (!ok) {
         tc_commit(drain);
         mbar_wait_drain(drain, 0, 200000000ull);
+      }
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ O += P V issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_o = idesc_f16(128, 64, false, true);   // B = V, MN-major
+      bool ok = true;
+      for (int jj = 0; ok && jj < nkv; ++jj) {
+        const int st = jj % KV_STAGES;
+        const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
+        for (int i = 0; i < 2; ++i) {
+          if (!mbar_wait(&p_full[i], jj & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+          if (i == 0 && !mbar_wait(&v_full[st], (jj / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_f16_ts(tmem + COL_O0 + i * 64, tmem + COL_P0 + i * 64 + k * 8, sdesc_sw128(v_addr + k * 2048),
+                       idesc_o, (jj > 0 || k > 0) ? 1u : 0u);
+          tc_commit(&o_done[i]);
+        }
+        if (ok) tc_commit(&v_empty[st]);
+      }
+      if (!ok) {
+        tc_commit(drain2);
+        mbar_wait_drain(drain2, 0, 200000000ull);
       }
     }
     }
