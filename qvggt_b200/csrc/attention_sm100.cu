@@ -509,13 +509,13 @@ extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, 
   const long long grid = (long long)a.nqb * heads * batches;
   if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
   // Share of exponentials computed on the FMA pipe (pairs per 8).  Measured
-  // on B200 with the chunked P stores: 0 is fastest (757 TFLOP/s at L=16384
-  // vs 713-723 for 1-2); the QVGGT_ATTN_POLY environment variable (0..4)
-  // overrides the default.
+  // on B200 with the split S / PV issuers: 1 is fastest at the aggregator's
+  // L = 43,968 (811 TFLOP/s vs 780 for 0 and 800 for 2); the QVGGT_ATTN_POLY
+  // environment variable (0..4) overrides the default.
   static int poly = -1;
   if (poly < 0) {
     const char* e = getenv("QVGGT_ATTN_POLY");
-    poly = (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 0;
+    poly = (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 1;
   }
   auto kfn = poly == 0 ? attn_fwd_kernel<0> : poly == 1 ? attn_fwd_kernel<1> : poly == 2 ? attn_fwd_kernel<2>
            : poly == 3 ? attn_fwd_kernel<3> : attn_fwd_kernel<4>;
