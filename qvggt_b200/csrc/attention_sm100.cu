@@ -227,6 +227,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const long long q_row0 = (long long)b * a.Lq + (long long)qb * 256;   // first query row of this CTA
   const long long kv_row0 = (long long)b * a.Lkv;
   const int nkv = a.nkv;
+  // Q tiles of this CTA that hold rows of its batch (the last block of a
+  // batch may end inside tile 0, e.g. 1374 = 5 x 256 + 94): an empty tile 1
+  // gets no MMAs and no softmax.
+  const int nqt = ((long long)qb * 256 + 128 < a.Lq) ? 2 : 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int st = j % KV_STAGES;
         if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
         const uint32_t k_addr = smem_u32(smem + AttnSmem::K + st * TILE_BYTES);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < nqt; ++i) {
           if (j > 0 && !mbar_wait(&s_free[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) {
             ok = false;
             break;
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int jj = 0; ok && jj < nkv; ++jj) {
         const int st = jj % KV_STAGES;
         const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < nqt; ++i) {
           if (!mbar_wait(&p_full[i], jj & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
           if (i == 0 && !mbar_wait(&v_full[st], (jj / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
             ok = false;
@@ -372,8 +376,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tO = tmem + lane_base + COL_O0 + i * 64;
     const float c = a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
+    bool ok = i < nqt;
+    for (int j = 0; ok && j < nkv; ++j) {
       if (!mbar_wait_warp(&s_full[i], j & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[128];
