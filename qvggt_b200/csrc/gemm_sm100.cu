@@ -397,15 +397,15 @@ int gemm_launch(const GemmLaunch& L) {
   const bool bn256 = (L.N % 256 == 0) && !L.force_bn128;
   // CTA pairs (2-SM MMA, 256-row tiles) once there are enough rows to fill
   // them.  Chosen per mode by measurement on B200 at the aggregator shapes
-  // (M = 43968, N = 4096, K = 1024): dense fp16 1228 vs 1085 TFLOP/s on pairs;
-  // W4A16 762 vs 836 and int8 1202 vs 1220 stay on the 1-SM kernel.
+  // (M = 43968, N = 4096, K = 1024): dense fp16 1213 vs 1078 TFLOP/s and
+  // W4A16 906 vs 825 on pairs; int8 1187 vs 1216 stays on the 1-SM kernel.
   // QVGGT_GEMM_2SM=0 / =1 forces one kernel for every mode.
   static int force_2sm = -2;
   if (force_2sm == -2) {
     const char* e = getenv("QVGGT_GEMM_2SM");
     force_2sm = (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
   }
-  const bool pair_mode = force_2sm >= 0 ? force_2sm == 1 : L.mode == B_F16;
+  const bool pair_mode = force_2sm >= 0 ? force_2sm == 1 : (L.mode == B_F16 || L.mode == B_W4);
   if (pair_mode && bn256 && L.M >= 512) return gemm_launch_2sm(L);
   switch (L.mode) {
     case B_W4: return bn256 ? launch_gemm<256, B_W4>(L) : launch_gemm<128, B_W4>(L);

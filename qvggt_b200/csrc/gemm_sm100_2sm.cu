@@ -12,9 +12,12 @@
 //
 // Signalling across the pair: TMA loads of both CTAs complete on the even
 // CTA's `full` barrier; the MMA commits are multicast to both CTAs' `empty`,
-// `empty_d` and `tmem_full` barriers; dequant warps and epilogue warps of both
-// CTAs arrive on the even CTA's `full_d` / `tmem_empty` barriers (mapa
-// addresses).  Every wait is bounded; both CTAs meet in a cluster barrier
+// `empty_d` and `tmem_full` barriers; epilogue warps of both CTAs arrive on
+// the even CTA's `tmem_empty` barriers (mapa addresses).  W4: the dequant
+// warps arrive on a local `dq_done` barrier, and one forwarder thread per
+// dequant group (warps 2 and 3) turns that into a single arrival on the even
+// CTA's `full_d`: a cluster-scope release arrive costs its thread close to a
+// microsecond on B200, which the dequant warps must not wait out.  Every wait is bounded; both CTAs meet in a cluster barrier
 // before TMEM is freed and before either exits.  No multicast loads.
 #include "gemm_common.cuh"
 #include "gemm_sm100.cuh"
@@ -48,7 +51,7 @@ struct Cfg2 {
   // so that every operand read of the pair MMA stays inside this CTA's
   // allocation even for a full-width B tile.
   static constexpr int OFF_BAR = 0;
-  static constexpr int NUM_BARS = 4 * NS + 2 * ND + 4 + 1;
+  static constexpr int NUM_BARS = 4 * NS + 3 * ND + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_A = 1024;
   static constexpr int OFF_B = OFF_A + NS * A_BYTES;                        // dense B stages / W4 packed stages
@@ -77,6 +80,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   uint64_t* tmem_full = empty_d + C::ND;   // [2] MMA -> epilogue (multicast)
   uint64_t* tmem_empty = tmem_full + 2;    // [2] both CTAs' epilogue -> MMA (even CTA's copy)
   uint64_t* drain_bar = tmem_empty + 2;
+  uint64_t* dq_done = drain_bar + 1;       // [ND] local dequant warps -> local forwarder (W4)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -94,7 +98,8 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
       mbar_init(&empty_b[i], C::DQ_GROUP_WARPS > 0 ? C::DQ_GROUP_WARPS : 1);
     }
     for (int i = 0; i < C::ND; ++i) {
-      mbar_init(&full_d[i], 2 * C::DQ_GROUP_WARPS);
+      mbar_init(&full_d[i], 2);                      // one forwarded arrival per CTA
+      mbar_init(&dq_done[i], C::DQ_GROUP_WARPS);
       mbar_init(&empty_d[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -223,6 +228,26 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
         mbar_wait_drain(drain_bar, 0, 200000000ull);
       }
     }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ W4: dequant -> MMA forwarders
+    // Warp 2 forwards the k-blocks of dequant group 0 (it % 2 == 0), warp 3
+    // those of group 1, in the dequant warps' order.
+    if constexpr (MODE == B_W4) {
+      if (lane == 0) {
+        const uint32_t group = (uint32_t)(warp - 2);
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters) {
+          for (int kb = 0; kb < num_kb; ++kb, ++it) {
+            if ((it & 1u) != group) continue;
+            const int d = it % C::ND;
+            const uint32_t dph = (it / C::ND) & 1;
+            if (!mbar_wait(&dq_done[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+            mbar_arrive_cluster(mapa_shared(&full_d[d], 0));
+          }
+        }
+      }
+    }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp - 4;
@@ -297,7 +322,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(&full_d[d], 0));
+          if (lane == 0) mbar_arrive(&dq_done[d]);
         }
         if (!ok) break;
       }
