@@ -214,6 +214,16 @@ int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_
                     int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
                     int32_t heads, void* stream);
 
+/* Attention over short sequences with head_dim 128 (the camera-head trunk:
+ * 16 heads x 128 over the S <= 256 camera tokens of each batch),
+ * softmax(q k^T / sqrt(128)) v on CUDA cores in fp32.  Same token-major
+ * layout as qvggt_attention with heads at column h*128 and Lq = Lkv = L.
+ * New entry point (the reference model runs PyTorch SDPA in its camera head,
+ * loader.py:338-344 quantises the trunk's linears around it). */
+int qvggt_attention_small(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                          int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t L, int32_t heads,
+                          void* stream);
+
 /* ---------------------------------------------------------- patch embed */
 
 /* images fp16 [S, 3, H, W] (pixels in [0, 1]) -> patches fp16

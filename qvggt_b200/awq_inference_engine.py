@@ -25,7 +25,7 @@ __all__ = [
     "gemm_forward_cuda_new", "gemv_forward_cuda_new", "w8a8_gemm_forward_cuda",
     "w8a8_gemm_fuse_bias_forward_cuda", "invoke_quant", "rms_norm_general", "gelu_and_quant",
     "fused_rope_with_pos_forward_func", "w4a16_linear", "f16_linear", "layernorm", "qkv_rope2d",
-    "attention", "i8_gemm_i32", "small_linear",
+    "attention", "attention_small", "i8_gemm_i32", "small_linear",
 ]
 
 
@@ -446,6 +446,24 @@ def assemble_tokens(src, src_rows_per_frame: int, src_row_offset: int, specials,
 
 
 F16_ = torch.float16
+
+
+def attention_small(q, kv, heads: int, batches: int, L: int, out=None, k_col0: int | None = None,
+                    v_col0: int | None = None):
+    """Attention with head_dim 128 over L <= 256 tokens per batch (camera-head
+    trunk): q [batches*L, heads*128], kv rows holding k and v (by default
+    kv = [k | v]).  Returns out [batches*L, heads*128]."""
+    name = "attention_small"
+    dev = _check_cuda(name, q, kv)
+    Cd = heads * 128
+    if out is None:
+        out = torch.empty(batches * L, Cd, dtype=torch.float16, device=dev)
+    k0 = 0 if k_col0 is None else k_col0
+    v0 = Cd if v_col0 is None else v_col0
+    with _Dev(dev):
+        _lib.call("qvggt_attention_small", _ptr(q), q.stride(0), _ptr(kv), kv.stride(0), k0, v0, _ptr(out),
+                  out.stride(0), batches, L, heads, _stream(q))
+    return out
 
 
 def attention(q, kv, heads: int, batches: int, Lq: int, Lkv: int, out=None, k_col0: int | None = None,

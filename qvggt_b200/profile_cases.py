@@ -5,6 +5,7 @@
     python -m qvggt_b200.profile_cases mem                    # LayerNorm, invoke_quant, GEMV
     python -m qvggt_b200.profile_cases small [M] [N] [K]      # small-M split-K GEMM (camera trunk)
     python -m qvggt_b200.profile_cases small_time             # small-M vs large kernel vs GEMV
+    python -m qvggt_b200.profile_cases trunk                  # camera-head trunk (4 blocks, width 2048)
     python -m qvggt_b200.profile_cases time                   # CUDA-event timings of all of the above
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
@@ -136,6 +137,20 @@ def small_time():
             print("  ".join(row))
 
 
+def trunk_time():
+    """Camera-head trunk forward (4 W4A16 blocks of width 2048) over S camera
+    tokens, CUDA-graph replay; the per-block algorithmic work is
+    2 * S * 2048 * (6144 + 2048 + 8192 + 8192) + 4 * S^2 * 2048 FLOP."""
+    from .camera_trunk import random_camera_trunk
+    trunk = random_camera_trunk(seed=1, device="cuda", depth=4)
+    for S in (8, 32, 64, 200):
+        x = torch.randn(1, S, 2048, device="cuda").half()
+        t = _time(lambda: trunk(x), 20, graph=True)
+        fl = 4 * (2 * S * 2048 * (6144 + 2048 + 8192 + 8192) + 4 * S * S * 2048)
+        wbytes = 4 * 2048 * (6144 + 2048 + 8192 + 8192) // 2
+        print(f"camera trunk S={S}: {t * 1e6:.1f} us ({fl / t / 1e12:.2f} TFLOP/s, W4 weights {wbytes / t / 1e9:.0f} GB/s)")
+
+
 def _time(fn, iters=20, graph=False):
     """Average device time per call.  graph=True captures the `iters` calls in
     one CUDA graph first, so host launch overhead does not pace short kernels."""
@@ -178,6 +193,8 @@ def main(argv):
         small(*(int(v) for v in argv[1:4]))
     elif what == "small_time":
         small_time()
+    elif what == "trunk":
+        trunk_time()
     elif what == "time":
         for L, b in ((16384, 1), (43968, 1), (1374, 32)):
             fn, fl = attn(L, b)
