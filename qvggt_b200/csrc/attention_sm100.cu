@@ -49,7 +49,8 @@ struct AttnSmem {
   // o_done[2], drain (S issuer), drain2 (PV issuer)
   static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 2;
   static constexpr int MISC = BAR + NUM_BARS * 8;
-  static constexpr int TOTAL = MISC + 16 + 1024;
+  // MISC: +0 TMEM base, +4 abort flag, +8 status word pointer, +16 timeout (ns)
+  static constexpr int TOTAL = MISC + 24 + 1024;
 };
 
 struct AttnArgs {
@@ -65,6 +66,49 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Bounded mbarrier wait.  Its failure bookkeeping (abort flag, status word
+// pointer, timeout) is read from shared memory at `misc` only once the first
+// try_wait fails, so a thread keeps no registers for it across its loop (held
+// in registers, it pushed parts of a softmax thread's 128-score row to local
+// memory).
+__device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, uint32_t misc, uint32_t code) {
+  int ab;
+  uint64_t status, timeout;
+  asm volatile("ld.shared.u64 %0, [%1 + 8];" : "=l"(status) : "r"(misc));
+  asm volatile("ld.shared.u64 %0, [%1 + 16];" : "=l"(timeout) : "r"(misc));
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+    asm volatile("ld.volatile.shared.s32 %0, [%1 + 4];" : "=r"(ab) : "r"(misc) : "memory");
+    if (ab) return false;
+#pragma unroll 1
+    for (int k = 0; k < 16; ++k)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > timeout) {
+      asm volatile("st.volatile.shared.s32 [%0 + 4], 1;" ::"r"(misc) : "memory");
+      if (status) atomicCAS(reinterpret_cast<uint32_t*>(status), 0u, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, uint32_t misc, uint32_t code) {
+  return mbar_try_wait(bar, parity) || wait_slow(bar, parity, misc, code);
+}
+__device__ __forceinline__ bool wait(const uint64_t* bar, uint32_t parity, uint32_t misc, uint32_t code) {
+  return wait(smem_u32(bar), parity, misc, code);
+}
+
+// The softmax warps' wait (barrier given by its shared-memory address): all
+// lanes wait; the warp proceeds only if all saw the phase complete.
+__device__ __forceinline__ bool softmax_wait(uint32_t bar, uint32_t parity, uint32_t misc) {
+  return __all_sync(0xffffffffu, wait(bar, parity, misc, ST_TIMEOUT_SOFTMAX));
+}
+
+__device__ __forceinline__ void arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // tcgen05.ld writes its destination registers asynchronously: they are valid
@@ -177,13 +221,13 @@ __device__ __forceinline__ void exp_chunk(uint32_t (&s)[128], uint64_t c2, uint6
 // sum of P, or NaN if the wait gave up.
 template <bool PARTIAL, int POLY>
 __device__ __forceinline__ float exp_store(uint32_t (&s)[128], float c, float neg_m, int valid, uint32_t tP,
-                                           bool o_ready, uint64_t* o_done, uint32_t o_parity,
-                                           volatile int* abort_flag, const Ctl& ctl) {
+                                           bool o_ready, uint32_t o_done, uint32_t o_parity,
+                                           uint32_t misc) {
   const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(neg_m, neg_m);
   uint64_t l2 = f2_pack(0.f, 0.f);
   exp_chunk<PARTIAL, POLY, 0>(s, c2, nm2, l2, valid);
   if (!o_ready) {
-    if (!mbar_wait_warp(o_done, o_parity, abort_flag, ctl, ST_TIMEOUT_SOFTMAX)) return __int_as_float(0x7fc00000);
+    if (!softmax_wait(o_done, o_parity, misc)) return __int_as_float(0x7fc00000);
     tc_fence_after();
   }
   tmem_st16(tP + 0, *reinterpret_cast<const uint32_t(*)[16]>(&s[0]));
@@ -211,6 +255,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* v_full = k_full + KV_STAGES;
   uint64_t* k_empty = v_full + KV_STAGES;   // [S] MMA -> K producer: S_0, S_1 of the tile done
   uint64_t* v_empty = k_empty + KV_STAGES;  // [S] MMA -> V producer: PV_0, PV_1 of the tile done
+  // the four [2] arrays below are consecutive: the softmax warps address them
+  // from s_full[i] at byte offsets 16, 32 and 48
   uint64_t* s_full = v_empty + KV_STAGES;   // [2] MMA -> softmax: S_i ready
   uint64_t* s_free = s_full + 2;            // [2] softmax -> MMA: S_i read
   uint64_t* p_full = s_free + 2;            // [2] softmax -> MMA: P_i written
@@ -249,6 +295,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(drain2, 1);
     *abort_flag = 0;
+    *reinterpret_cast<uint32_t**>(smem + AttnSmem::MISC + 8) = a.ctl.status;
+    *reinterpret_cast<unsigned long long*>(smem + AttnSmem::MISC + 16) = a.ctl.timeout_ns;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -264,6 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t misc = smem_u32(smem + AttnSmem::MISC);
 
   // Registers: launched at 168 per thread (384 x 168 = 64512); warpgroup 0
   // (producer, MMA, two idle warps) gives back to 56, the two softmax
@@ -290,7 +339,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (; j < nkv; ++j) {
         const int st = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
-        if (!mbar_wait(&empty[st], ph ^ 1, abort_flag, a.ctl, ST_TIMEOUT_TMA_EMPTY)) break;
+        if (!wait(&empty[st], ph ^ 1, misc, ST_TIMEOUT_TMA_EMPTY)) break;
         const int row = (int)(kv_row0 + (long long)j * 128);
         mbar_arrive_expect_tx(&full[st], TILE_BYTES);
         tma_load_3d(base + st * TILE_BYTES, tm, &full[st], 0, h, row);
@@ -311,13 +360,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, 128);
       const uint32_t q_addr[2] = {smem_u32(smem + AttnSmem::Q0), smem_u32(smem + AttnSmem::Q1)};
-      bool ok = mbar_wait(q_full, 0, abort_flag, a.ctl, ST_TIMEOUT_FULL);
+      bool ok = wait(q_full, 0, misc, ST_TIMEOUT_FULL);
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % KV_STAGES;
-        if (!mbar_wait(&k_full[st], (j / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+        if (!wait(&k_full[st], (j / KV_STAGES) & 1, misc, ST_TIMEOUT_FULL)) { ok = false; break; }
         const uint32_t k_addr = smem_u32(smem + AttnSmem::K + st * TILE_BYTES);
         for (int i = 0; i < nqt; ++i) {
-          if (j > 0 && !mbar_wait(&s_free[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) {
+          if (j > 0 && !wait(&s_free[i], (j - 1) & 1, misc, ST_TIMEOUT_SOFTMAX)) {
             ok = false;
             break;
           }
@@ -344,8 +393,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int st = jj % KV_STAGES;
         const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
         for (int i = 0; i < nqt; ++i) {
-          if (!mbar_wait(&p_full[i], jj & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
-          if (i == 0 && !mbar_wait(&v_full[st], (jj / KV_STAGES) & 1, abort_flag, a.ctl, ST_TIMEOUT_FULL)) {
+          if (!wait(&p_full[i], jj & 1, misc, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+          if (i == 0 && !wait(&v_full[st], (jj / KV_STAGES) & 1, misc, ST_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
@@ -375,60 +424,73 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tP = tmem + lane_base + COL_P0 + i * 64;
     const uint32_t tO = tmem + lane_base + COL_O0 + i * 64;
     const float c = a.scale_log2;
+    const uint32_t bar_s_full = smem_u32(&s_full[i]);
+    const uint32_t bar_s_free = bar_s_full + 16, bar_p_full = bar_s_full + 32, bar_o_done = bar_s_full + 48;
+    // keys in the last KV tile (the others are full)
+    const int last_valid = (int)(a.Lkv - (long long)(nkv - 1) * 128);
     float m_used = -INFINITY, l = 0.f;
     bool ok = i < nqt;
     for (int j = 0; ok && j < nkv; ++j) {
-      if (!mbar_wait_warp(&s_full[i], j & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+      if (!softmax_wait(bar_s_full, j & 1, misc)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[128];
       load_s_row(tS, s);
       // S_i is in registers: hand the TMEM columns back to the MMA warp
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[i]);
+      if (lane == 0) arrive(bar_s_free);
 
-      const long long rem = a.Lkv - (long long)j * 128;
-      const int valid = rem >= 128 ? 128 : (int)rem;
+      const int valid = j + 1 < nkv ? 128 : last_valid;
       const float mx = (valid == 128) ? row_max<false>(s, valid) : row_max<true>(s, valid);
       const float m_new = fmaxf(m_used, mx * c);
       const bool need = m_new > m_used + 8.0f;
-      bool o_ready = (j == 0);   // PV_i(j-1) complete (nothing to wait for at j = 0)
+      // Raising m rescales O_i and l by alpha; O_i is rescaled after the P
+      // store, when PV_i(j-1) is known complete and the scores are no longer
+      // held in registers.
+      float alpha = 1.f;
+      bool rescale = false;
       if (__any_sync(0xffffffffu, need)) {
         const float m_target = need ? m_new : m_used;
-        const float alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_target);
-        if (j > 0) {
-          if (!mbar_wait_warp(&o_done[i], (j - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
-          o_ready = true;
-          tc_fence_after();
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t v[16];
-            tmem_ld16(tO + cc * 16, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st16(tO + cc * 16, v);
-          }
-        }
-        l *= alpha;
+        alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_target);
+        rescale = j > 0;
         m_used = m_target;
       }
       const uint32_t o_par = (uint32_t)(j - 1) & 1;
+      const bool o_ready = j == 0;   // PV_i(j-1) complete (nothing to wait for at j = 0)
       const float lj = (valid == 128)
-          ? exp_store<false, POLY>(s, c, -m_used, valid, tP, o_ready, &o_done[i], o_par, abort_flag, a.ctl)
-          : exp_store<true, POLY>(s, c, -m_used, valid, tP, o_ready, &o_done[i], o_par, abort_flag, a.ctl);
+          ? exp_store<false, POLY>(s, c, -m_used, valid, tP, o_ready, bar_o_done, o_par, misc)
+          : exp_store<true, POLY>(s, c, -m_used, valid, tP, o_ready, bar_o_done, o_par, misc);
       if (__any_sync(0xffffffffu, lj != lj)) { ok = false; break; }
-      l += lj;
+      l = l * alpha + lj;
+      if (rescale) {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[16];
+          tmem_ld16(tO + cc * 16, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st16(tO + cc * 16, v);
+        }
+        tmem_st_wait();
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[i]);
+      if (lane == 0) arrive(bar_p_full);
     }
     if (ok && nkv > 0) {
-      if (mbar_wait_warp(&o_done[i], (nkv - 1) & 1, abort_flag, a.ctl, ST_TIMEOUT_SOFTMAX)) {
+      if (softmax_wait(bar_o_done, (nkv - 1) & 1, misc)) {
         tc_fence_after();
-        const long long qr = (long long)qb * 256 + i * 128 + r;   // row within the batch
+        // the CTA's coordinates are re-derived here (a volatile read of
+        // %ctaid.x) rather than kept in registers through the loop
+        uint32_t cta;
+        asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(cta));
+        const int qb_e = (int)(cta % (uint32_t)a.nqb);
+        const int h_e = (int)((cta / (uint32_t)a.nqb) % (uint32_t)a.heads);
+        const long long b_e = cta / ((uint32_t)a.nqb * (uint32_t)a.heads);
+        const long long qr = (long long)qb_e * 256 + i * 128 + r;   // row within the batch
         const float inv = 1.f / l;
-        __half* dst = a.out + (q_row0 + i * 128 + r) * a.o_stride + h * 64;
+        __half* dst = a.out + (b_e * a.Lq + qr) * a.o_stride + h_e * 64;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t v[16];

@@ -29,12 +29,15 @@ struct GemmArgs {
 // then for q / k heads the optional per-head LayerNorm and the 2-D RoPE of the
 // VGGT aggregator (dims 0..31 rotated by the patch row, 32..63 by the patch
 // column, rotate-half pairs i <-> i+16, h(h(x*cos) + h(rot*sin))), stored to
-// q_out or kv_out.
+// q_out or kv_out.  Every intermediate y is an fp16 value, so the head is held
+// as 32 packed half2 words (yh[k] = y[2k], y[2k+1]): the arithmetic is the
+// same fp32 sequence, at half the registers (the W4 GEMM runs 512 threads
+// with 128 registers each).
 __device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, int col0, const uint32_t (&r)[64]) {
   const RopeEpi& R = g.rope;
   const int region = col0 / R.dim;           // 0 = q, 1 = k, 2 = v
   const int hcol = col0 - region * R.dim;    // column of the head inside its region
-  float y[64];
+  uint32_t yh[32];
   const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col0);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -43,8 +46,8 @@ __device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, in
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 b = unpack_half2(b4[e]);
-      y[8 * j + 2 * e] = round_f16(round_f16(__uint_as_float(r[8 * j + 2 * e])) + b.x);
-      y[8 * j + 2 * e + 1] = round_f16(round_f16(__uint_as_float(r[8 * j + 2 * e + 1])) + b.y);
+      yh[4 * j + e] = pack_half2(round_f16(__uint_as_float(r[8 * j + 2 * e])) + b.x,
+                                 round_f16(__uint_as_float(r[8 * j + 2 * e + 1])) + b.y);
     }
   }
   __half* dst;
@@ -59,15 +62,28 @@ __device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, in
     if (nw) {
       float s = 0.f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) s += y[i];
+      for (int k = 0; k < 32; ++k) {
+        const float2 y = unpack_half2(yh[k]);
+        s += y.x;
+        s += y.y;
+      }
       const float mean = s * (1.f / 64.f);
       float q = 0.f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) q = fmaf(y[i] - mean, y[i] - mean, q);
+      for (int k = 0; k < 32; ++k) {
+        const float2 y = unpack_half2(yh[k]);
+        q = fmaf(y.x - mean, y.x - mean, q);
+        q = fmaf(y.y - mean, y.y - mean, q);
+      }
       const float rstd = rsqrtf(q * (1.f / 64.f) + R.eps);
+      const uint32_t* nw2 = reinterpret_cast<const uint32_t*>(nw);
+      const uint32_t* nb2 = reinterpret_cast<const uint32_t*>(nb);
 #pragma unroll
-      for (int i = 0; i < 64; ++i)
-        y[i] = round_f16(fmaf((y[i] - mean) * rstd, __half2float(__ldg(nw + i)), __half2float(__ldg(nb + i))));
+      for (int k = 0; k < 32; ++k) {
+        const float2 y = unpack_half2(yh[k]);
+        const float2 w = unpack_half2(__ldg(nw2 + k)), b = unpack_half2(__ldg(nb2 + k));
+        yh[k] = pack_half2(fmaf((y.x - mean) * rstd, w.x, b.x), fmaf((y.y - mean) * rstd, w.y, b.y));
+      }
     }
     const int p = (int)(((long long)row + R.token_offset) % R.tokens_per_frame);
     int py = 0, px = 0;
@@ -79,7 +95,8 @@ __device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, in
     const __half* ct = reinterpret_cast<const __half*>(R.cos_tab);
     const __half* st = reinterpret_cast<const __half*>(R.sin_tab);
     // The tables hold each angle twice (columns i and i+16 are equal), so the
-    // pair (i, i+16) shares one cos / sin: rotate it in place.
+    // pair (i, i+16) shares one cos / sin: rotate it in place.  Columns i and
+    // i+1 (i even) are one packed word, as are i+16 and i+17.
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int pp = half ? px : py;
@@ -89,22 +106,21 @@ __device__ __forceinline__ void epilogue_qkv_head(const GemmArgs& g, int row, in
         const uint4 su = __ldg(reinterpret_cast<const uint4*>(st + pp * 32) + j);
         const uint32_t c4[4] = {cu.x, cu.y, cu.z, cu.w}, s4[4] = {su.x, su.y, su.z, su.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int i = 32 * half + 8 * j + e;
-          const float2 c2 = unpack_half2(c4[e / 2]), s2 = unpack_half2(s4[e / 2]);
-          const float cs = (e & 1) ? c2.y : c2.x, sn = (e & 1) ? s2.y : s2.x;
-          const float a = y[i], bq = y[i + 16];
-          y[i] = round_f16(round_f16(a * cs) + round_f16(-bq * sn));
-          y[i + 16] = round_f16(round_f16(bq * cs) + round_f16(a * sn));
+        for (int e = 0; e < 4; ++e) {
+          const int k = 16 * half + 4 * j + e;   // word of columns 2k, 2k+1; its partner is word k+8
+          const float2 cs = unpack_half2(c4[e]), sn = unpack_half2(s4[e]);
+          const float2 a = unpack_half2(yh[k]), bq = unpack_half2(yh[k + 8]);
+          yh[k] = pack_half2(round_f16(a.x * cs.x) + round_f16(-bq.x * sn.x),
+                             round_f16(a.y * cs.y) + round_f16(-bq.y * sn.y));
+          yh[k + 8] = pack_half2(round_f16(bq.x * cs.x) + round_f16(a.x * sn.x),
+                                 round_f16(bq.y * cs.y) + round_f16(a.y * sn.y));
         }
       }
     }
   }
   uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
-    d4[j] = make_uint4(pack_half2(y[8 * j], y[8 * j + 1]), pack_half2(y[8 * j + 2], y[8 * j + 3]),
-                       pack_half2(y[8 * j + 4], y[8 * j + 5]), pack_half2(y[8 * j + 6], y[8 * j + 7]));
+  for (int j = 0; j < 8; ++j) d4[j] = make_uint4(yh[4 * j], yh[4 * j + 1], yh[4 * j + 2], yh[4 * j + 3]);
 }
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }

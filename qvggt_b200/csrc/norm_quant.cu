@@ -192,23 +192,28 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32) gelu_quant_kernel(const _
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROWS_PER_BLOCK + (threadIdx.x >> 5);
   if (row >= T) return;
-  __half t[CH * 8];
+  // GELU outputs kept as packed half2 words (an array of 16-bit halves was
+  // placed in local memory)
+  uint32_t t2[CH * 4];
   float amax = 0.f;
   const __half zero = __float2half_rn(0.0001f);
 #pragma unroll
   for (int j = 0; j < CH; ++j) {
     uint4 u = *reinterpret_cast<const uint4*>(x + row * H + (j * 32 + lane) * 8);
-    const __half* hx = reinterpret_cast<const __half*>(&u);
-    __half o[8];
+    const uint32_t xw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const __half g = gelu_fast_h(hx[e]);
-      t[j * 8 + e] = g;
-      o[e] = g;
-      const __half a = __hgt(g, zero) ? g : __hneg(g);
-      amax = fmaxf(amax, __half2float(a));
+    for (int e = 0; e < 4; ++e) {
+      const __half2 hx = *reinterpret_cast<const __half2*>(&xw[e]);
+      const __half g0 = gelu_fast_h(__low2half(hx)), g1 = gelu_fast_h(__high2half(hx));
+      const __half2 g = __halves2half2(g0, g1);
+      t2[j * 4 + e] = *reinterpret_cast<const uint32_t*>(&g);
+      const __half a0 = __hgt(g0, zero) ? g0 : __hneg(g0);
+      const __half a1 = __hgt(g1, zero) ? g1 : __hneg(g1);
+      amax = fmaxf(amax, __half2float(a0));
+      amax = fmaxf(amax, __half2float(a1));
     }
-    *reinterpret_cast<uint4*>(tmp + row * H + (j * 32 + lane) * 8) = *reinterpret_cast<uint4*>(o);
+    *reinterpret_cast<uint4*>(tmp + row * H + (j * 32 + lane) * 8) =
+        make_uint4(t2[j * 4], t2[j * 4 + 1], t2[j * 4 + 2], t2[j * 4 + 3]);
   }
   amax = warp_max(amax);
   if (lane == 0) scale[row] = __float2half_rn(amax / 127.f);
@@ -220,8 +225,11 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32) gelu_quant_kernel(const _
     for (int q = 0; q < 2; ++q) {
       uint32_t pk = 0;
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        pk |= (uint32_t)(uint8_t)f32_to_s8_rni_sat(__half2float(__hmul(hs, t[j * 8 + 4 * q + e]))) << (8 * e);
+      for (int e = 0; e < 2; ++e) {
+        const __half2 g = *reinterpret_cast<const __half2*>(&t2[j * 4 + 2 * q + e]);
+        pk |= (uint32_t)(uint8_t)f32_to_s8_rni_sat(__half2float(__hmul(hs, __low2half(g)))) << (16 * e);
+        pk |= (uint32_t)(uint8_t)f32_to_s8_rni_sat(__half2float(__hmul(hs, __high2half(g)))) << (16 * e + 8);
+      }
       o[q] = pk;
     }
     *reinterpret_cast<uint2*>(out + row * H + (j * 32 + lane) * 8) = make_uint2(o[0], o[1]);
