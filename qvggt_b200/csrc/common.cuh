@@ -293,6 +293,20 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t cluster_addr) {
   return v;
 }
 // Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA).
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// this CTA's shared memory to a shared::cluster address, completing `bytes`
+// transactions on the mbarrier at the shared::cluster address `mbar`.  No
+// multicast.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                     uint32_t mbar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
+               : "memory");
+}
+// 32-bit store to distributed shared memory (any CTA of the cluster).
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }

@@ -15,10 +15,16 @@
 // `empty_d` and `tmem_full` barriers; epilogue warps of both CTAs arrive on
 // the even CTA's `tmem_empty` barriers (mapa addresses).  W4: the dequant
 // warps arrive on a local `dq_done` barrier, and one forwarder thread per
-// dequant group (warps 2 and 3) turns that into a single arrival on the even
-// CTA's `full_d`: a cluster-scope release arrive costs its thread close to a
-// microsecond on B200, which the dequant warps must not wait out.  Every wait is bounded; both CTAs meet in a cluster barrier
-// before TMEM is freed and before either exits.  No multicast loads.
+// dequant group (warps 2 and 3) turns that into a 16-byte DSMEM bulk copy
+// (cp.async.bulk shared::cta -> shared::cluster) that completes its bytes on
+// the even CTA's `full_d`, armed by the MMA thread with expect_tx for both
+// CTAs' copies.  The MMA thread therefore waits on `full_d` exactly as on the
+// TMA-completed `full` barrier, at CTA scope: a cluster-scope acquire cost it
+// ~0.15 us per k-block, and a cluster-scope release arrive costs its thread
+// close to a microsecond.  Every wait is bounded; both CTAs meet in a cluster barrier
+// before TMEM is freed and before either exits; a CTA that aborted also
+// marks its peer and both pause before exit so that no bulk copy in flight
+// outlives its source or destination.  No multicast loads.
 #include "gemm_common.cuh"
 #include "gemm_sm100.cuh"
 #include "host.hpp"
@@ -59,7 +65,9 @@ struct Cfg2 {
   static constexpr int OFF_SZ = OFF_D + ND * B_BYTES;
   static constexpr int END = OFF_SZ + NS * SZ_BYTES;
   static constexpr int SMEM = END + HBN * KBB + 1024;                       // + guard + alignment slack
-  static_assert(OFF_MISC + 16 <= OFF_A, "barrier region overflow");
+  static constexpr int OFF_SIG = 768;                                       // 2 x 16 B bulk-copy slots (W4)
+  static constexpr uint32_t SIG_BYTES = 16;
+  static_assert(OFF_MISC + 16 <= OFF_SIG && OFF_SIG + 2 * 16 <= OFF_A, "barrier region overflow");
   static constexpr uint32_t TMEM_COLS = 2 * PBN;                            // 512: two accumulators
 };
 
@@ -98,7 +106,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
       mbar_init(&empty_b[i], C::DQ_GROUP_WARPS > 0 ? C::DQ_GROUP_WARPS : 1);
     }
     for (int i = 0; i < C::ND; ++i) {
-      mbar_init(&full_d[i], 2);                      // one forwarded arrival per CTA
+      mbar_init(&full_d[i], 1);                      // the MMA thread's expect_tx arrival
       mbar_init(&dq_done[i], C::DQ_GROUP_WARPS);
       mbar_init(&empty_d[i], 1);
     }
@@ -108,6 +116,9 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
+    // first phase of each full_d: both CTAs' signal copies
+    if (leader)
+      for (int i = 0; i < C::ND; ++i) mbar_arrive_expect_tx(&full_d[i], 2 * C::SIG_BYTES);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -206,7 +217,11 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           if (!mbar_wait(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           uint64_t bd;
           if constexpr (MODE == B_W4) {
-            if (!mbar_wait_cluster(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+            // completes through both CTAs' signal copies (complete_tx):
+            // CTA scope, like `full`; then arm the buffer's next phase (its
+            // copies come only after the commit below frees the buffer)
+            if (!mbar_wait(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full_d[d], 2 * C::SIG_BYTES);
             bd = b_desc0 + (uint64_t)((d * C::B_BYTES) >> 4);
           } else {
             bd = b_desc0 + (uint64_t)((s * C::B_BYTES) >> 4);
@@ -242,6 +257,8 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     if constexpr (MODE == B_W4) {
       if (lane == 0) {
         const uint32_t group = (uint32_t)(warp - 2);
+        const uint32_t sig_src = smem_u32(smem + C::OFF_SIG + rank * 16);
+        const uint32_t sig_dst = mapa_shared(smem + C::OFF_SIG + rank * 16, 0);
         uint32_t it = 0;
         bool ok = true;
         for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters) {
@@ -250,7 +267,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
             const int d = it % C::ND;
             const uint32_t dph = (it / C::ND) & 1;
             if (!mbar_wait(&dq_done[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
-            mbar_arrive_cluster(mapa_shared(&full_d[d], 0));
+            bulk_copy_to_cluster(sig_dst, sig_src, C::SIG_BYTES, mapa_shared(&full_d[d], 0));
           }
         }
       }
@@ -338,10 +355,21 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // An abort in either CTA marks both, so both see it after the cluster barrier.
+  if (threadIdx.x == 0 && *abort_flag) st_cluster_u32(mapa_shared(const_cast<int*>(abort_flag), rank ^ 1u), 1u);
   cluster_sync();   // neither CTA frees TMEM or exits while its peer may still use the pair
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (MODE == B_W4) {
+    // After an abort, W4 signal copies issued before the cluster barrier may
+    // still be in flight: let them land before either CTA exits.
+    if (*abort_flag) {
+      const uint64_t t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 50000ull) {
+      }
+    }
   }
 }
 

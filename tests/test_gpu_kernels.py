@@ -382,3 +382,21 @@ def test_pair_gemm_equals_single_sm_gemm(mode):
         full, part = f(x), f(x[:384].contiguous())
         assert awq.max_abs_rel(full.cpu(), ref) <= 2e-3
     assert torch.equal(full[:384], part)
+
+
+def test_w4_pair_gemm_equals_f16_pair_gemm_on_dequantised_weights():
+    """The W4 pair kernel dequantises each CTA's half of B in shared memory and
+    hands it to the pair MMA through a DSMEM bulk-copy signal; the fp16 pair
+    kernel gets the same B halves by TMA.  With the exactly dequantised weights
+    (fp16) the two must agree bit for bit, on every repetition (a stale B half
+    would show up as a mismatch)."""
+    from qvggt_b200 import awq_inference_engine as eng
+    M, N, K, G = 4096, 4096, 1024, 128
+    lin, t = _lin(N, K, G, seed=41)
+    w16 = torch.from_numpy(awq.dequantize(lin["qweight"], lin["scales"], lin["scaled_zeros"], G)).half().to(DEV)
+    g = torch.Generator().manual_seed(43)
+    for _ in range(6):
+        x = torch.randn(M, K, generator=g).half().to(DEV)
+        y4 = eng.gemm_forward_cuda_new(x, t["qweight"], t["scales"], t["scaled_zeros"], group_size=G)
+        y16 = eng.f16_linear(x, w16)
+        assert torch.equal(y4, y16)
