@@ -11,20 +11,22 @@
 // work, while each SM still double-buffers its 2 x 256 accumulator columns.
 //
 // Signalling across the pair: TMA loads of both CTAs complete on the even
-// CTA's `full` barrier; the MMA commits are multicast to both CTAs' `empty`,
-// `empty_d` and `tmem_full` barriers; epilogue warps of both CTAs arrive on
-// the even CTA's `tmem_empty` barriers (mapa addresses).  W4: the dequant
-// warps arrive on a local `dq_done` barrier, and one forwarder thread per
-// dequant group (warps 2 and 3) turns that into a 16-byte DSMEM bulk copy
-// (cp.async.bulk shared::cta -> shared::cluster) that completes its bytes on
-// the even CTA's `full_d`, armed by the MMA thread with expect_tx for both
-// CTAs' copies.  The MMA thread therefore waits on `full_d` exactly as on the
-// TMA-completed `full` barrier, at CTA scope: a cluster-scope acquire cost it
-// ~0.15 us per k-block, and a cluster-scope release arrive costs its thread
-// close to a microsecond.  Every wait is bounded; both CTAs meet in a cluster barrier
-// before TMEM is freed and before either exits; a CTA that aborted also
-// marks its peer and both pause before exit so that no bulk copy in flight
-// outlives its source or destination.  No multicast loads.
+// CTA's `full` barrier; the MMA commits are multicast to both CTAs' `empty`
+// and `tmem_full` barriers; epilogue warps of both CTAs arrive on the even
+// CTA's `tmem_empty` barriers (mapa addresses).  W4: dequantisation buffer d
+// of k-block j is free once the MMAs of k-block j - ND are done, which the
+// dequant warps read from that k-block's `empty` barrier (no barrier or commit
+// of its own).  Each dequant warp then signals the even CTA with a 16-byte
+// DSMEM bulk copy (cp.async.bulk shared::cta -> shared::cluster) that
+// completes its bytes on `full_d[d]`, armed by the MMA thread with expect_tx
+// for all eight warps' copies; the even CTA's warps first wait for both CTAs'
+// A tiles (`full`), so the MMA thread waits on `full_d` alone, at CTA scope
+// like on a TMA-completed barrier.  (A cluster-scope acquire cost the MMA
+// thread ~0.15 us per k-block, and a cluster-scope release arrive costs its
+// thread close to a microsecond.)  Every wait is bounded; both CTAs meet in a
+// cluster barrier before TMEM is freed and before either exits; a CTA that
+// aborted also marks its peer and both pause before exit so that no bulk copy
+// in flight outlives its source or destination.  No multicast loads.
 #include "gemm_common.cuh"
 #include "gemm_sm100.cuh"
 #include "host.hpp"
@@ -57,7 +59,12 @@ struct Cfg2 {
   // so that every operand read of the pair MMA stays inside this CTA's
   // allocation even for a full-width B tile.
   static constexpr int OFF_BAR = 0;
-  static constexpr int NUM_BARS = 4 * NS + 3 * ND + 4 + 1;
+  static constexpr int NUM_BARS = 4 * NS + ND + 4 + 1;
+  // W4: buffer d = j % ND is reused by k-block j once the MMAs of j - ND are
+  // done, read from empty[(j - ND) % NS].  NS - ND even and positive: the next
+  // phase of that barrier needs the MMAs of j - ND + NS, whose B the same
+  // dequant group produces after k-block j, so the parity wait cannot alias.
+  static_assert(MODE != B_W4 || (NS > ND && (NS - ND) % 2 == 0), "W4 buffer reuse needs NS - ND even, > 0");
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_A = 1024;
   static constexpr int OFF_B = OFF_A + NS * A_BYTES;                        // dense B stages / W4 packed stages
@@ -65,9 +72,10 @@ struct Cfg2 {
   static constexpr int OFF_SZ = OFF_D + ND * B_BYTES;
   static constexpr int END = OFF_SZ + NS * SZ_BYTES;
   static constexpr int SMEM = END + HBN * KBB + 1024;                       // + guard + alignment slack
-  static constexpr int OFF_SIG = 768;                                       // 2 x 16 B bulk-copy slots (W4)
+  static constexpr int OFF_SIG = 768;                                       // 16 B bulk-copy slot per dequant warp
   static constexpr uint32_t SIG_BYTES = 16;
-  static_assert(OFF_MISC + 16 <= OFF_SIG && OFF_SIG + 2 * 16 <= OFF_A, "barrier region overflow");
+  static constexpr uint32_t SIG_TX = 2 * DQ_GROUP_WARPS * SIG_BYTES;        // both CTAs' copies per k-block
+  static_assert(OFF_MISC + 16 <= OFF_SIG && OFF_SIG + 2 * NUM_DQ_WARPS * 16 <= OFF_A, "barrier region overflow");
   static constexpr uint32_t TMEM_COLS = 2 * PBN;                            // 512: two accumulators
 };
 
@@ -83,12 +91,10 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   uint64_t* empty = bars + C::NS;          // [NS] MMA -> producers (multicast)
   uint64_t* full_b = bars + 2 * C::NS;     // [NS] local TMA -> local dequant (W4)
   uint64_t* empty_b = bars + 3 * C::NS;    // [NS] local dequant -> local producer (W4)
-  uint64_t* full_d = bars + 4 * C::NS;     // [ND] both CTAs' dequant -> MMA (even CTA's copy)
-  uint64_t* empty_d = full_d + C::ND;      // [ND] MMA -> dequant (multicast)
-  uint64_t* tmem_full = empty_d + C::ND;   // [2] MMA -> epilogue (multicast)
+  uint64_t* full_d = bars + 4 * C::NS;     // [ND] both CTAs' dequant warps -> MMA (even CTA's copy)
+  uint64_t* tmem_full = full_d + C::ND;    // [2] MMA -> epilogue (multicast)
   uint64_t* tmem_empty = tmem_full + 2;    // [2] both CTAs' epilogue -> MMA (even CTA's copy)
   uint64_t* drain_bar = tmem_empty + 2;
-  uint64_t* dq_done = drain_bar + 1;       // [ND] local dequant warps -> local forwarder (W4)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -107,8 +113,6 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     }
     for (int i = 0; i < C::ND; ++i) {
       mbar_init(&full_d[i], 1);                      // the MMA thread's expect_tx arrival
-      mbar_init(&dq_done[i], C::DQ_GROUP_WARPS);
-      mbar_init(&empty_d[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tmem_full[i], 1);
@@ -118,7 +122,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     *abort_flag = 0;
     // first phase of each full_d: both CTAs' signal copies
     if (leader)
-      for (int i = 0; i < C::ND; ++i) mbar_arrive_expect_tx(&full_d[i], 2 * C::SIG_BYTES);
+      for (int i = 0; i < C::ND; ++i) mbar_arrive_expect_tx(&full_d[i], C::SIG_TX);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -140,9 +144,15 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = g.num_kb;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer (both CTAs)
+  if (warp == 0 || (MODE == B_W4 && warp == 2)) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    // Warp 0 loads A (and, dense / int8, B) into the stage ring paced by the
+    // MMAs (`empty`).  W4: warp 2 loads the packed weights, scales and zeros
+    // on their own pace, released by the dequant warps as soon as they have
+    // read them (`empty_b`), so the dequantisation of a k-block never waits
+    // behind the A tile of an earlier one.
     if (lane == 0) {
+      const bool b_role = MODE == B_W4 && warp == 2;
       uint32_t it = 0;
       bool ok = true;
       for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters) {
@@ -152,13 +162,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % C::NS;
           const uint32_t ph = (it / C::NS) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
-          const uint32_t full_lead = mapa_shared(&full[s], 0);
-          uint8_t* sa = smem + C::OFF_A + s * C::A_BYTES;
-          const int kx = kb * KBB / (MODE == B_I8 ? 1 : 2);
-          if constexpr (MODE == B_W4) {
-            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
-            tma_load_2d_pair(sa, &tmA, full_lead, kx, row0);
+          if (b_role) {
             if (!mbar_wait(&empty_b[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
             uint8_t* sq = smem + C::OFF_B + s * C::BQ_BYTES;
             uint8_t* ssz = smem + C::OFF_SZ + s * C::SZ_BYTES;
@@ -167,6 +171,15 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
             tma_load_2d(sq, &tmB, &full_b[s], kb * 64, col0 / 4);
             tma_load_2d(ssz, &tmS, &full_b[s], col0, grp);
             tma_load_2d(ssz + HBN * 2, &tmZ, &full_b[s], col0, grp);
+            continue;
+          }
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+          const uint32_t full_lead = mapa_shared(&full[s], 0);
+          uint8_t* sa = smem + C::OFF_A + s * C::A_BYTES;
+          const int kx = kb * KBB / (MODE == B_I8 ? 1 : 2);
+          if constexpr (MODE == B_W4) {
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
+            tma_load_2d_pair(sa, &tmA, full_lead, kx, row0);
           } else {
             uint8_t* sb = smem + C::OFF_B + s * C::B_BYTES;
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES));
@@ -177,15 +190,15 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
       }
       if (!ok) {
         // Let loads already issued land before this CTA can exit: wait for the
-        // stage barriers this CTA can observe (its own empty barriers of the
-        // last phases -- the MMA side has aborted too -- and, in W4 mode, the
-        // local full_b barriers).
+        // stage barriers this CTA can observe (the A producer: the even CTA's
+        // full barriers of the last phases -- the MMA side has aborted too;
+        // the W4 weight producer: the local full_b barriers).
         const uint32_t issued = it;
         for (int s = 0; s < C::NS; ++s) {
           const uint32_t cnt = issued > (uint32_t)s ? (issued - 1 - s) / C::NS + 1 : 0;
           if (cnt == 0) continue;
-          if (leader) mbar_wait_drain(&full[s], (cnt - 1) & 1, 200000000ull);
-          if constexpr (MODE == B_W4) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
+          if (b_role) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
+          else if (leader) mbar_wait_drain(&full[s], (cnt - 1) & 1, 200000000ull);
         }
       }
     }
@@ -213,15 +226,17 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
         for (int kb = 0; kb < num_kb; ++kb) {
           // `full` completes through both CTAs' TMA transactions (complete_tx,
           // no software arrivals): a CTA-scope wait suffices, and a
-          // cluster-scope acquire costs ~0.2 us per k-block on B200.
-          if (!mbar_wait(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+          // cluster-scope acquire costs ~0.2 us per k-block on B200.  In W4
+          // mode the even CTA's dequant warps have waited on it before
+          // signalling full_d.
+          if (MODE != B_W4 && !mbar_wait(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           uint64_t bd;
           if constexpr (MODE == B_W4) {
             // completes through both CTAs' signal copies (complete_tx):
             // CTA scope, like `full`; then arm the buffer's next phase (its
             // copies come only after the commit below frees the buffer)
             if (!mbar_wait(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
-            mbar_arrive_expect_tx(&full_d[d], 2 * C::SIG_BYTES);
+            mbar_arrive_expect_tx(&full_d[d], C::SIG_TX);
             bd = b_desc0 + (uint64_t)((d * C::B_BYTES) >> 4);
           } else {
             bd = b_desc0 + (uint64_t)((s * C::B_BYTES) >> 4);
@@ -237,7 +252,6 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           }
           tc_commit_pair(&empty[s], 3);
           if constexpr (MODE == B_W4) {
-            tc_commit_pair(&empty_d[d], 3);
             if (++d == C::ND) { d = 0; dph ^= 1; }
           }
           if (++s == C::NS) { s = 0; ph ^= 1; }
@@ -248,28 +262,6 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
       if (!ok) {
         tc_commit(drain_bar);
         mbar_wait_drain(drain_bar, 0, 200000000ull);
-      }
-    }
-  } else if (warp == 2 || warp == 3) {
-    // ------------------------------------------------------------ W4: dequant -> MMA forwarders
-    // Warp 2 forwards the k-blocks of dequant group 0 (it % 2 == 0), warp 3
-    // those of group 1, in the dequant warps' order.
-    if constexpr (MODE == B_W4) {
-      if (lane == 0) {
-        const uint32_t group = (uint32_t)(warp - 2);
-        const uint32_t sig_src = smem_u32(smem + C::OFF_SIG + rank * 16);
-        const uint32_t sig_dst = mapa_shared(smem + C::OFF_SIG + rank * 16, 0);
-        uint32_t it = 0;
-        bool ok = true;
-        for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters) {
-          for (int kb = 0; kb < num_kb; ++kb, ++it) {
-            if ((it & 1u) != group) continue;
-            const int d = it % C::ND;
-            const uint32_t dph = (it / C::ND) & 1;
-            if (!mbar_wait(&dq_done[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
-            bulk_copy_to_cluster(sig_dst, sig_src, C::SIG_BYTES, mapa_shared(&full_d[d], 0));
-          }
-        }
       }
     }
   } else if (warp >= 4 && warp < 8) {
@@ -316,6 +308,9 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
       const int n = dq % HBN;           // local output channel, 0..HBN-1
       const int grow = n >> 2;
       const int ci = n & 3;
+      const int slot = (int)rank * C::NUM_DQ_WARPS + (warp - 8);
+      const uint32_t sig_src = smem_u32(smem + C::OFF_SIG + slot * 16);
+      const uint32_t sig_dst = mapa_shared(smem + C::OFF_SIG + slot * 16, 0);
       uint32_t it = 0;
       for (int tile = cluster; tile < g.num_tiles; tile += num_clusters) {
         bool ok = true;
@@ -334,8 +329,14 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty_b[s]);
           const int d = it % C::ND;
-          const uint32_t dph = (it / C::ND) & 1;
-          if (!mbar_wait_warp(&empty_d[d], dph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
+          // buffer d is free once the MMAs of k-block it - ND are done
+          if (it >= (uint32_t)C::ND) {
+            const uint32_t jf = it - C::ND;
+            if (!mbar_wait_warp(&empty[jf % C::NS], (jf / C::NS) & 1, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) {
+              ok = false;
+              break;
+            }
+          }
           uint8_t* drow = smem + C::OFF_D + d * C::B_BYTES + n * 128;
           uint4 o[4];
           dequant_chunk(x0, s2, z2, o);
@@ -345,8 +346,11 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
           fence_proxy_async_smem();
+          // the even CTA's warps also take the wait for both CTAs' A tiles
+          // off the MMA thread
+          if (leader && !mbar_wait_warp(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&dq_done[d]);
+          if (lane == 0) bulk_copy_to_cluster(sig_dst, sig_src, C::SIG_BYTES, mapa_shared(&full_d[d], 0));
         }
         if (!ok) break;
       }
