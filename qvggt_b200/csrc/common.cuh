@@ -112,8 +112,11 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 // ---------------------------------------------------------------------------
 // Proxy fences
 // ---------------------------------------------------------------------------
-// Make this thread's generic-proxy shared-memory writes visible to the async
-// proxy (tcgen05.mma operand reads, TMA stores).
+// Order this thread's generic-proxy shared-memory accesses before later
+// async-proxy accesses: writes that tcgen05.mma or a TMA store will read
+// (RAW), and reads of a TMA-filled buffer that is about to be released for the
+// next TMA load into it (WAR: without it, a stage released right after
+// ordinary loads was observed overwritten before the loads had read it).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -326,6 +326,8 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           *reinterpret_cast<uint4*>(x1) = *reinterpret_cast<const uint4*>(sq + (((2 * ci + 1) ^ (grow & 7)) * 16));
           const __half2 s2 = __half2half2(ssz[n]);
           const __half2 z2 = __half2half2(ssz[HBN + n]);
+          // the stage is refilled by TMA once released: retire these reads first
+          fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty_b[s]);
           const int d = it % C::ND;
