@@ -62,3 +62,18 @@ def test_attention_strided_views():
     vh = qkv[:, 2 * C:].reshape(1, L, heads, 64).permute(0, 2, 1, 3)
     ref = om.sdpa(qh, kh, vh).permute(0, 2, 1, 3).reshape(L, C)
     assert awq.rel_l2(out, ref) <= 4e-3
+
+
+def test_attention_repeatable_bit_for_bit():
+    """Every output element is reduced in one fixed order (one CTA per query
+    block, KV tiles in sequence), so repeated calls agree bit for bit; a race
+    between the warp roles (an S, P or O buffer used before its hand-off)
+    would show up as a difference between calls."""
+    from qvggt_b200 import awq_inference_engine as eng
+    g = torch.Generator(device=DEV).manual_seed(5)
+    batches, L, heads = 1, 8192, 16
+    q = torch.randn(batches * L, heads * 64, generator=g, device=DEV).half()
+    kv = torch.randn(batches * L, 2 * heads * 64, generator=g, device=DEV).half()
+    first = eng.attention(q, kv, heads, batches, L, L)
+    for _ in range(8):
+        assert torch.equal(eng.attention(q, kv, heads, batches, L, L), first)
