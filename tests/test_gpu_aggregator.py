@@ -102,3 +102,25 @@ def test_two_pairs_end_to_end():
         x = g
     assert awq.rel_l2(outs[-1][1].view(S, P, C).cpu(), x) <= 2e-2
     assert awq.rel_l2(outs[-1][1].view(S, P, C).cpu().float() - tokens.float(), x.float() - tokens.float()) <= 2e-2
+
+
+def test_loaded_checkpoint_runs_identically():
+    """An aggregator written to the VGGT checkpoint key layout and loaded back
+    (``qvggt_b200.loader``) runs the same kernels on the same weights: its
+    forward equals the original's bit for bit."""
+    import os
+    import tempfile
+    from qvggt_b200 import loader as L
+    from qvggt_b200.aggregator import AggConfig
+    from qvggt_b200.synthetic import random_vggt_aggregator, synthetic_images
+    cfg = AggConfig(dim=256, heads=4, depth=2, qk_norm=True)
+    agg = random_vggt_aggregator(cfg, 11, "cuda", 2, pe_depth=1)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "ckpt.pt")
+        torch.save(L.state_dict_from_aggregator(agg), path)
+        agg2 = L.load_aggregator(path, 2, "cuda", original_path=path, cfg=cfg)
+    imgs = synthetic_images(2, 5).cuda()
+    a = agg.forward(imgs)[-1][1].clone()
+    b = agg2.forward(imgs)[-1][1]
+    assert torch.isfinite(a.float()).all()
+    assert torch.equal(a, b)
