@@ -303,3 +303,11 @@ def state_dict_from_aggregator(agg: VGGTAggregator) -> OrderedDict:
     sd["aggregator.camera_token"] = agg.agg_specials[:, :1].reshape(1, 2, 1, C).cpu()
     sd["aggregator.register_token"] = agg.agg_specials[:, 1:].reshape(1, 2, -1, C).cpu()
     return sd
+
+
+def state_dict_from_camera_trunk(trunk, prefix: str = "camera_head.trunk") -> OrderedDict:
+    """The camera trunk's weights under ``camera_head.trunk.N.*``."""
+    sd = OrderedDict()
+    for i, b in enumerate(trunk.blocks):
+        _put_block(sd, f"{prefix}.{i}", b)
+    return sd

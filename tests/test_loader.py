@@ -119,3 +119,17 @@ def test_missing_or_gapped_blocks_raise():
     gap = OrderedDict((k, v) for k, v in sd.items() if not k.startswith("aggregator.frame_blocks.0."))
     with pytest.raises(KeyError):
         L.aggregator_from_state_dict(gap, 1, "cpu", cfg=cfg)
+
+
+def test_camera_trunk_round_trip_cpu():
+    from qvggt_b200.camera_trunk import CameraTrunk
+    from qvggt_b200.synthetic import random_block
+    gen = torch.Generator().manual_seed(9)
+    cfg = AggConfig(dim=256, heads=2)
+    trunk = CameraTrunk([random_block(cfg, gen, "cpu", "w4") for _ in range(2)])
+    sd = L.state_dict_from_camera_trunk(trunk)
+    assert L.infer_quantization_layout(sd)["quantize_camera_head"] is True
+    t2 = L.camera_trunk_from_state_dict(OrderedDict(("model." + k, v) for k, v in sd.items()), "cpu")
+    assert len(t2.blocks) == 2
+    for x, y in zip(trunk.blocks, t2.blocks):
+        _blocks_equal(x, y)
