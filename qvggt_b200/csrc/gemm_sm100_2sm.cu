@@ -13,7 +13,11 @@
 // Signalling across the pair: TMA loads of both CTAs complete on the even
 // CTA's `full` barrier; the MMA commits are multicast to both CTAs' `empty`
 // and `tmem_full` barriers; epilogue warps of both CTAs arrive on the even
-// CTA's `tmem_empty` barriers (mapa addresses).  W4: dequantisation buffer d
+// CTA's `tmem_empty` barriers (mapa addresses).  W4: the packed weights,
+// scales and zeros come through their own stage ring and producer warp
+// (warp 2); the dequant warps release a stage (`empty_b`) after a proxy fence
+// that retires their ordinary loads of it, since the next TMA refills it.
+// Dequantisation buffer d
 // of k-block j is free once the MMAs of k-block j - ND are done, which the
 // dequant warps read from that k-block's `empty` barrier (no barrier or commit
 // of its own).  Each dequant warp then signals the even CTA with a 16-byte
