@@ -6,6 +6,7 @@
     python -m qvggt_b200.profile_cases small [M] [N] [K]      # small-M split-K GEMM (camera trunk)
     python -m qvggt_b200.profile_cases small_time             # small-M vs large kernel vs GEMV
     python -m qvggt_b200.profile_cases trunk                  # camera-head trunk (4 blocks, width 2048)
+    python -m qvggt_b200.profile_cases forward w4|w8 [S] [n]  # whole aggregator forward, frames/s
     python -m qvggt_b200.profile_cases time                   # CUDA-event timings of all of the above
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
@@ -151,6 +152,26 @@ def trunk_time():
         print(f"camera trunk S={S}: {t * 1e6:.1f} us ({fl / t / 1e12:.2f} TFLOP/s, W4 weights {wbytes / t / 1e9:.0f} GB/s)")
 
 
+def forward_time(kind="w4", S=32, steps=3):
+    """Frames/s of the full aggregator forward (DINOv2 front + 24 pairs) on one
+    GPU, images resident: kind "w4" is BASELINE config 2, "w8" (S = 64) the
+    W8A8 aggregator of config 3."""
+    from .aggregator import AggConfig
+    from .synthetic import random_vggt_aggregator, synthetic_images
+    agg = random_vggt_aggregator(AggConfig(), 0, "cuda", S, kind=kind)
+    imgs = synthetic_images(S, 0).cuda()
+    agg.forward(imgs)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record()
+    for _ in range(steps):
+        agg.forward(imgs)
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / steps / 1e3
+    print(f"aggregator forward {kind} S={S}: {t * 1e3:.1f} ms, {S / t:.2f} frames/s")
+
+
 def _time(fn, iters=20, graph=False):
     """Average device time per call.  graph=True captures the `iters` calls in
     one CUDA graph first, so host launch overhead does not pace short kernels."""
@@ -195,6 +216,8 @@ def main(argv):
         small_time()
     elif what == "trunk":
         trunk_time()
+    elif what == "forward":
+        forward_time(argv[1] if len(argv) > 1 else "w4", *(int(v) for v in argv[2:4]))
     elif what == "time":
         for L, b in ((16384, 1), (43968, 1), (1374, 32)):
             fn, fl = attn(L, b)

@@ -99,15 +99,16 @@ def random_patch_embed(cfg: AggConfig, gen: torch.Generator, device, depth: int 
 
 
 def random_vggt_aggregator(cfg: AggConfig, seed: int, device, frames_local: int, group=None, world: int = 1,
-                           rank: int = 0, pe_depth: int = 24):
-    """Full synthetic VGGT-1B aggregator: DINOv2 front in
-    fp16 + ``cfg.depth`` W4A16 frame/global pairs, identical on every rank."""
+                           rank: int = 0, pe_depth: int = 24, kind: str = "w4"):
+    """Full synthetic VGGT-1B aggregator: DINOv2 front in fp16 + ``cfg.depth``
+    frame/global pairs with ``kind`` linears ("w4": BASELINE config 2, "w8":
+    the W8A8 chain of config 3), identical on every rank."""
     from .aggregator import VGGTAggregator
     gen = torch.Generator(device=device).manual_seed(seed)
     pe = random_patch_embed(cfg, gen, device, depth=pe_depth)
     specials = (torch.randn(2, cfg.patch_start, cfg.dim, generator=gen, device=device) * 0.02).to(F16).contiguous()
-    frame = [random_block(cfg, gen, device, "w4") for _ in range(cfg.depth)]
-    glob = [random_block(cfg, gen, device, "w4") for _ in range(cfg.depth)]
+    frame = [random_block(cfg, gen, device, kind) for _ in range(cfg.depth)]
+    glob = [random_block(cfg, gen, device, kind) for _ in range(cfg.depth)]
     return VGGTAggregator(cfg, pe, specials, frame, glob, frames_local, device, group, world, rank)
 
 
