@@ -402,3 +402,18 @@ def test_w4_pair_gemm_equals_f16_pair_gemm_on_dequantised_weights(M, N):
         y4 = eng.gemm_forward_cuda_new(x, t["qweight"], t["scales"], t["scaled_zeros"], group_size=G)
         y16 = eng.f16_linear(x, w16)
         assert torch.equal(y4, y16)
+
+
+def test_w4_single_sm_gemm_equals_f16_on_dequantised_weights():
+    """The 1-SM kernel (256 < M < 512 rows) dequantises through the same
+    stage-release protocol as the pair kernel: bit-equal to the fp16 kernel on
+    the exactly dequantised weights, on every repetition."""
+    from qvggt_b200 import awq_inference_engine as eng
+    M, N, K, G = 500, 3072, 1024, 128
+    lin, t = _lin(N, K, G, seed=43)
+    w16 = torch.from_numpy(awq.dequantize(lin["qweight"], lin["scales"], lin["scaled_zeros"], G)).half().to(DEV)
+    g = torch.Generator().manual_seed(47)
+    for _ in range(8):
+        x = torch.randn(M, K, generator=g).half().to(DEV)
+        y4 = eng.gemm_forward_cuda_new(x, t["qweight"], t["scales"], t["scaled_zeros"], group_size=G)
+        assert torch.equal(y4, eng.f16_linear(x, w16))
