@@ -88,12 +88,18 @@ def build(reference: str) -> str:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("QVGGT_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: QVGGT_REFERENCE, else BASELINE.json's reference_path)")
+    ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
-    if not os.path.isdir(a.reference):
+    if a.reference is None:
+        sys.path.insert(0, os.path.dirname(HERE))
+        from oracle.refpath import reference_path
+        a.reference = reference_path()
+    if not a.reference or not os.path.isdir(a.reference):
         print("reference checkout not present; oracle/_ref not built", file=sys.stderr)
         sys.exit(0)
-    if built_path() is not None and "--force" not in sys.argv:
+    if built_path() is not None and not a.force:
         print(built_path())
         sys.exit(0)
     print(build(a.reference))

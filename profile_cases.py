@@ -1,13 +1,13 @@
 """Small, fixed workloads of single kernels for profiling (ncu) and timing.
 
-    python -m qvggt_b200.profile_cases attn  [L] [batches]   # flash attention, 16 heads x 64
-    python -m qvggt_b200.profile_cases gemm  f16|w4|w8 [M]    # tcgen05 GEMM, N=4096 K=1024
-    python -m qvggt_b200.profile_cases mem                    # LayerNorm, invoke_quant, GEMV
-    python -m qvggt_b200.profile_cases small [M] [N] [K]      # small-M split-K GEMM (camera trunk)
-    python -m qvggt_b200.profile_cases small_time             # small-M vs large kernel vs GEMV
-    python -m qvggt_b200.profile_cases trunk                  # camera-head trunk (4 blocks, width 2048)
-    python -m qvggt_b200.profile_cases forward w4|w8 [S] [n]  # whole aggregator forward, frames/s
-    python -m qvggt_b200.profile_cases time                   # CUDA-event timings of all of the above
+    python profile_cases.py attn  [L] [batches]   # flash attention, 16 heads x 64
+    python profile_cases.py gemm  f16|w4|w8 [M]    # tcgen05 GEMM, N=4096 K=1024
+    python profile_cases.py mem                    # LayerNorm, invoke_quant, GEMV
+    python profile_cases.py small [M] [N] [K]      # small-M split-K GEMM (camera trunk)
+    python profile_cases.py small_time             # small-M vs large kernel vs GEMV
+    python profile_cases.py trunk                  # camera-head trunk (4 blocks, width 2048)
+    python profile_cases.py forward w4|w8 [S] [n]  # whole aggregator forward, frames/s
+    python profile_cases.py time                   # CUDA-event timings of all of the above
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
 launch) on seeded synthetic data sized above the 126 MB L2 where it matters.
@@ -18,12 +18,16 @@ import sys
 
 import torch
 
-from . import _lib
-from . import awq_inference_engine as eng
+import os
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from qvggt_b200 import _lib  # noqa: E402
+from qvggt_b200 import awq_inference_engine as eng  # noqa: E402
 
 
 def _w4(N, K, seed=1):
-    from .synthetic import quantize_w4
+    from qvggt_b200.synthetic import quantize_w4
     g = torch.Generator(device="cuda").manual_seed(seed)
     w = torch.randn(N, K, generator=g, device="cuda") * 0.02
     return quantize_w4(w, 128)
@@ -142,7 +146,7 @@ def trunk_time():
     """Camera-head trunk forward (4 W4A16 blocks of width 2048) over S camera
     tokens, CUDA-graph replay; the per-block algorithmic work is
     2 * S * 2048 * (6144 + 2048 + 8192 + 8192) + 4 * S^2 * 2048 FLOP."""
-    from .camera_trunk import random_camera_trunk
+    from qvggt_b200.camera_trunk import random_camera_trunk
     trunk = random_camera_trunk(seed=1, device="cuda", depth=4)
     for S in (8, 32, 64, 200):
         x = torch.randn(1, S, 2048, device="cuda").half()
@@ -156,8 +160,8 @@ def forward_time(kind="w4", S=32, steps=3):
     """Frames/s of the full aggregator forward (DINOv2 front + 24 pairs) on one
     GPU, images resident: kind "w4" is BASELINE config 2, "w8" (S = 64) the
     W8A8 aggregator of config 3."""
-    from .aggregator import AggConfig
-    from .synthetic import random_vggt_aggregator, synthetic_images
+    from qvggt_b200.aggregator import AggConfig
+    from qvggt_b200.synthetic import random_vggt_aggregator, synthetic_images
     agg = random_vggt_aggregator(AggConfig(), 0, "cuda", S, kind=kind)
     imgs = synthetic_images(S, 0).cuda()
     agg.forward(imgs)

@@ -62,6 +62,50 @@ def _contig(name, *ts):
             raise ValueError(f"{name}: tensors must be contiguous")
 
 
+def _check_shape(name, cond: bool, what: str):
+    if not cond:
+        raise ValueError(f"{name}: {what}")
+
+
+def _check_w4_weights(name, qweight, scales, scaled_zeros, K: int, group_size: int):
+    """qweight int16 [N/4, K]; scales / scaled_zeros fp16 [gpad, N] with at
+    least K / group_size group rows (the kernels read that many)."""
+    _check_dtype(name, qweight, torch.int16)
+    _check_dtype(name, scales, torch.float16)
+    _check_dtype(name, scaled_zeros, torch.float16)
+    _check_shape(name, qweight.dim() == 2 and qweight.shape[1] == K,
+                 f"qweight {tuple(qweight.shape)} must be [N/4, K={K}]")
+    N = qweight.shape[0] * 4
+    _check_shape(name, group_size > 0 and K % group_size == 0, f"K={K} is not a multiple of group_size={group_size}")
+    for t, n in ((scales, "scales"), (scaled_zeros, "scaled_zeros")):
+        _check_shape(name, t.dim() == 2 and t.shape[1] == N and t.shape[0] >= K // group_size,
+                     f"{n} {tuple(t.shape)} must be [>= {K // group_size}, N={N}]")
+    return N
+
+
+def _check_epilogue(name, M: int, N: int, bias=None, residual=None, gamma=None, out=None):
+    """bias / gamma fp16 with >= N entries; residual / out fp16 contiguous [.., N] with M rows."""
+    for t, n in ((bias, "bias"), (gamma, "gamma")):
+        if t is not None:
+            _check_dtype(name, t, torch.float16)
+            _check_shape(name, t.numel() >= N, f"{n} has {t.numel()} entries, needs {N}")
+    for t, n in ((residual, "residual"), (out, "out")):
+        if t is not None:
+            _check_dtype(name, t, torch.float16)
+            _contig(name, t)
+            _check_shape(name, t.shape[-1] == N and t.numel() == M * N,
+                         f"{n} {tuple(t.shape)} must hold {M} rows of N={N}")
+
+
+def _check_rows(name, t, rows: int, cols: int, what: str):
+    """A row-major fp16 operand read through its row stride: 2-D, unit column
+    stride, at least `rows` rows and `cols` columns."""
+    _check_dtype(name, t, torch.float16)
+    _check_shape(name, t.dim() == 2 and t.stride(-1) == 1 and t.shape[0] >= rows and t.shape[1] >= cols,
+                 f"{what} {tuple(t.shape)} (strides {tuple(t.stride())}) must be a row-major view with >= {rows} "
+                 f"rows and >= {cols} columns")
+
+
 class _Dev:
     def __init__(self, dev):
         self.g = torch.cuda.device(dev)
@@ -84,14 +128,9 @@ def gemm_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, group_size: i
     name = "gemm_forward_cuda_new"
     dev = _check_cuda(name, in_feats, qweight, scales, scaled_zeros)
     _check_dtype(name, in_feats, torch.float16)
-    _check_dtype(name, scales, torch.float16)
-    _check_dtype(name, scaled_zeros, torch.float16)
-    _check_dtype(name, qweight, torch.int16)
     _contig(name, in_feats, qweight, scales, scaled_zeros)
     K = in_feats.shape[-1]
-    N = qweight.shape[0] * 4
-    if qweight.shape[1] != K:
-        raise ValueError(f"{name}: qweight {tuple(qweight.shape)} does not match K={K}")
+    N = _check_w4_weights(name, qweight, scales, scaled_zeros, K, group_size)
     M = in_feats.numel() // K
     out = torch.empty(*in_feats.shape[:-1], N, dtype=in_feats.dtype, device=dev)
     with _Dev(dev):
@@ -115,6 +154,10 @@ def gemv_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, m: int, n: in
         raise RuntimeError("Unsupported batch size for gemv kernel.")
     if group_size % 32 or k % group_size:
         raise RuntimeError("Unsupported group size for gemv kernel.")
+    _check_shape(name, in_feats.shape[-1] == k and in_feats.numel() >= m * k,
+                 f"in_feats {tuple(in_feats.shape)} must hold m={m} rows of k={k}")
+    _check_shape(name, _check_w4_weights(name, qweight, scales, scaled_zeros, k, group_size) == n,
+                 f"qweight {tuple(qweight.shape)} does not give n={n} channels")
     out = torch.empty(*in_feats.shape[:-1], n, dtype=in_feats.dtype, device=dev)
     with _Dev(dev):
         _lib.call("qvggt_w4a16_gemv", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
@@ -131,15 +174,20 @@ def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 
     ``SMALL_M_MAX`` rows the split-K small-M kernel, more the persistent
     tcgen05 GEMM."""
     name = "w4a16_linear"
-    dev = _check_cuda(name, x, qweight, scales, scaled_zeros, bias, residual, gamma)
+    dev = _check_cuda(name, x, qweight, scales, scaled_zeros, bias, residual, gamma, out)
+    _check_dtype(name, x, torch.float16)
     _contig(name, x, qweight, scales, scaled_zeros, bias, gamma)
     K = x.shape[-1]
-    N = qweight.shape[0] * 4
+    N = _check_w4_weights(name, qweight, scales, scaled_zeros, K, group_size)
     M = x.numel() // K
+    _check_epilogue(name, M, N, bias, residual, gamma, None if residual is not None else out)
+    _check_shape(name, residual is None or gamma is not None, "a residual update needs gamma")
     if residual is not None:
         out = residual
     elif out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
+    if M == 0:
+        return out
     with _Dev(dev):
         if M <= GEMV_M_MAX and act is None and residual is None:
             _lib.call("qvggt_w4a16_gemv", _ptr(x), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), _ptr(bias),
@@ -161,15 +209,25 @@ def qkv_rope_linear(x, lin, heads: int, cos_tab, sin_tab, tokens_per_frame: int 
     split and VGGT 2-D RoPE fused into the GEMM epilogue.
     Returns (q [M, C] roped, kv [M, 2C] = [k roped | v])."""
     name = "qkv_rope_linear"
-    dev = _check_cuda(name, x, lin.bias, cos_tab, sin_tab)
-    _contig(name, x, cos_tab, sin_tab)
+    dev = _check_cuda(name, x, lin.bias, cos_tab, sin_tab, q_out, kv_out)
+    _check_dtype(name, x, torch.float16)
+    _contig(name, x, cos_tab, sin_tab, q_out, kv_out)
     K = x.shape[-1]
     M = x.numel() // K
     Cd = heads * 64
+    if lin.kind == "w4":
+        N = _check_w4_weights(name, lin.qweight, lin.scales, lin.scaled_zeros, K, lin.group_size)
+    else:
+        _check_shape(name, lin.weight.dim() == 2 and lin.weight.shape[1] == K, "weight must be [3C, K]")
+        N = lin.weight.shape[0]
+    _check_shape(name, N == 3 * Cd, f"the qkv linear has {N} outputs, needs 3 * {Cd}")
+    _check_epilogue(name, M, N, lin.bias)
     if q_out is None:
         q_out = torch.empty(M, Cd, dtype=torch.float16, device=dev)
     if kv_out is None:
         kv_out = torch.empty(M, 2 * Cd, dtype=torch.float16, device=dev)
+    _check_epilogue(name, M, Cd, out=q_out)
+    _check_epilogue(name, M, 2 * Cd, out=kv_out)
     qn = qk_norm if qk_norm is not None else (None, None, None, None)
     if lin.kind == "w4":
         wk, b, s, z, gpad, G = 0, lin.qweight, lin.scales, lin.scaled_zeros, lin.scales.shape[0], lin.group_size
@@ -186,15 +244,22 @@ def qkv_rope_linear(x, lin, heads: int, cos_tab, sin_tab, tokens_per_frame: int 
 def f16_linear(x, weight, bias=None, act: str | None = None, residual=None, gamma=None, out=None):
     """Dense fp16 linear (weight [N, K]) with the same fused epilogues."""
     name = "f16_linear"
-    dev = _check_cuda(name, x, weight, bias, residual, gamma)
+    dev = _check_cuda(name, x, weight, bias, residual, gamma, out)
+    _check_dtype(name, x, torch.float16)
+    _check_dtype(name, weight, torch.float16)
     _contig(name, x, weight, bias, gamma)
     K = x.shape[-1]
+    _check_shape(name, weight.dim() == 2 and weight.shape[1] == K, f"weight {tuple(weight.shape)} must be [N, K={K}]")
     N = weight.shape[0]
     M = x.numel() // K
+    _check_epilogue(name, M, N, bias, residual, gamma, None if residual is not None else out)
+    _check_shape(name, residual is None or gamma is not None, "a residual update needs gamma")
     if residual is not None:
         out = residual
     elif out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=torch.float16, device=dev)
+    if M == 0:
+        return out
     with _Dev(dev):
         if 1 <= M <= SMALL_M_MAX:
             _small_linear(1, x, weight, None, None, 128, bias, out, M, N, K, 1 if act == "gelu" else 0,
@@ -234,12 +299,20 @@ def small_linear(x, weight, scales=None, scaled_zeros=None, bias=None, group_siz
     ``scales`` is given (``weight`` = qweight int16 [N/4, K]), else dense fp16
     ``weight`` [N, K].  Same epilogues and rounding as :func:`w4a16_linear`."""
     name = "small_linear"
-    dev = _check_cuda(name, x, weight, scales, scaled_zeros, bias, residual, gamma)
+    dev = _check_cuda(name, x, weight, scales, scaled_zeros, bias, residual, gamma, out)
+    _check_dtype(name, x, torch.float16)
     _contig(name, x, weight, scales, scaled_zeros, bias, gamma)
     kind = 0 if scales is not None else 1
     K = x.shape[-1]
-    N = weight.shape[0] * (4 if kind == 0 else 1)
+    if kind == 0:
+        N = _check_w4_weights(name, weight, scales, scaled_zeros, K, group_size)
+    else:
+        _check_dtype(name, weight, torch.float16)
+        _check_shape(name, weight.dim() == 2 and weight.shape[1] == K,
+                     f"weight {tuple(weight.shape)} must be [N, K={K}]")
+        N = weight.shape[0]
     M = x.numel() // K
+    _check_epilogue(name, M, N, bias, residual, gamma, None if residual is not None else out)
     if residual is not None:
         out = residual
     elif out is None:
@@ -256,9 +329,18 @@ def _w8a8(name, in_feats, kernel, wscales, ascales, out, bias):
     _check_dtype(name, in_feats, torch.int8)
     _check_dtype(name, kernel, torch.int8)
     _check_dtype(name, out, torch.float16)
+    _check_dtype(name, wscales, torch.float16)
+    _check_dtype(name, ascales, torch.float16)
+    _check_dtype(name, bias, torch.float16)
     _contig(name, in_feats, kernel, wscales, ascales, out, bias)
+    _check_shape(name, in_feats.dim() == 2, f"in_feats {tuple(in_feats.shape)} must be [M, K]")
     M, K = in_feats.shape[0], in_feats.shape[1]
     N = out.shape[-1]
+    _check_shape(name, tuple(kernel.shape) == (N, K), f"kernel {tuple(kernel.shape)} must be [N={N}, K={K}]")
+    _check_shape(name, out.numel() == M * N, f"out {tuple(out.shape)} must be [M={M}, N={N}]")
+    _check_shape(name, wscales.numel() >= N, f"wscales has {wscales.numel()} entries, needs N={N}")
+    _check_shape(name, ascales.numel() >= M, f"ascales has {ascales.numel()} entries, needs M={M}")
+    _check_shape(name, bias is None or bias.numel() >= N, f"bias needs N={N} entries")
     with _Dev(dev):
         _lib.call("qvggt_w8a8_gemm", _ptr(in_feats), _ptr(kernel), _ptr(wscales), _ptr(ascales), _ptr(bias),
                   _ptr(out), M, N, K, _stream(in_feats))
@@ -278,9 +360,19 @@ def w8a8_gemm_residual(in_feats, kernel, wscales, ascales, bias, gamma, residual
     """residual += half(half(W8A8 GEMM(+bias)) * gamma) (LayerScale residual fused)."""
     name = "w8a8_gemm_residual"
     dev = _check_cuda(name, in_feats, kernel, wscales, ascales, bias, gamma, residual)
+    _check_dtype(name, in_feats, torch.int8)
+    _check_dtype(name, kernel, torch.int8)
+    _check_dtype(name, wscales, torch.float16)
+    _check_dtype(name, ascales, torch.float16)
     _contig(name, in_feats, kernel, wscales, ascales, bias, gamma, residual)
+    _check_shape(name, in_feats.dim() == 2 and kernel.dim() == 2 and kernel.shape[1] == in_feats.shape[1],
+                 f"in_feats {tuple(in_feats.shape)} / kernel {tuple(kernel.shape)} must be [M, K] / [N, K]")
     M, K = in_feats.shape[0], in_feats.shape[1]
     N = kernel.shape[0]
+    _check_shape(name, wscales.numel() >= N, f"wscales has {wscales.numel()} entries, needs N={N}")
+    _check_shape(name, ascales.numel() >= M, f"ascales has {ascales.numel()} entries, needs M={M}")
+    _check_shape(name, gamma is not None, "gamma is required")
+    _check_epilogue(name, M, N, bias, residual, gamma)
     with _Dev(dev):
         _lib.call("qvggt_w8a8_gemm_residual", _ptr(in_feats), _ptr(kernel), _ptr(wscales), _ptr(ascales), _ptr(bias),
                   _ptr(gamma), _ptr(residual), M, N, K, _stream(in_feats))
@@ -291,7 +383,11 @@ def i8_gemm_i32(in_feats, kernel):
     """Raw int32 accumulators of the int8 GEMM (for bit-exact checks)."""
     name = "i8_gemm_i32"
     dev = _check_cuda(name, in_feats, kernel)
+    _check_dtype(name, in_feats, torch.int8)
+    _check_dtype(name, kernel, torch.int8)
     _contig(name, in_feats, kernel)
+    _check_shape(name, in_feats.dim() == 2 and kernel.dim() == 2 and kernel.shape[1] == in_feats.shape[1],
+                 f"in_feats {tuple(in_feats.shape)} / kernel {tuple(kernel.shape)} must be [M, K] / [N, K]")
     M, K = in_feats.shape
     N = kernel.shape[0]
     acc = torch.empty(M, N, dtype=torch.int32, device=dev)
@@ -381,11 +477,14 @@ def single_query_attention(*args, **kw):
 # ----------------------------------------------------------- new hot-path ops
 def layernorm(x, weight, bias, eps: float = 1e-6, out=None):
     name = "layernorm"
-    dev = _check_cuda(name, x, weight, bias)
-    _contig(name, x, weight, bias)
+    dev = _check_cuda(name, x, weight, bias, out)
+    _check_dtype(name, x, torch.float16)
+    _contig(name, x, weight, bias, out)
     H = x.shape[-1]
+    _check_shape(name, weight.numel() >= H and bias.numel() >= H, f"weight / bias need {H} entries")
     if out is None:
         out = torch.empty_like(x)
+    _check_shape(name, out.numel() == x.numel() and out.dtype == torch.float16, "out must match x")
     with _Dev(dev):
         _lib.call("qvggt_layernorm", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), x.numel() // H, H, float(eps),
                   _stream(x))
@@ -454,12 +553,15 @@ def attention_small(q, kv, heads: int, batches: int, L: int, out=None, k_col0: i
     trunk): q [batches*L, heads*128], kv rows holding k and v (by default
     kv = [k | v]).  Returns out [batches*L, heads*128]."""
     name = "attention_small"
-    dev = _check_cuda(name, q, kv)
+    dev = _check_cuda(name, q, kv, out)
     Cd = heads * 128
     if out is None:
         out = torch.empty(batches * L, Cd, dtype=torch.float16, device=dev)
     k0 = 0 if k_col0 is None else k_col0
     v0 = Cd if v_col0 is None else v_col0
+    _check_rows(name, q, batches * L, Cd, "q")
+    _check_rows(name, kv, batches * L, max(k0, v0) + Cd, "kv")
+    _check_rows(name, out, batches * L, Cd, "out")
     with _Dev(dev):
         _lib.call("qvggt_attention_small", _ptr(q), q.stride(0), _ptr(kv), kv.stride(0), k0, v0, _ptr(out),
                   out.stride(0), batches, L, heads, _stream(q))
@@ -471,12 +573,15 @@ def attention(q, kv, heads: int, batches: int, Lq: int, Lkv: int, out=None, k_co
     """Flash attention (head_dim 64) over token-major q [batches*Lq, heads*64]
     and kv [batches*Lkv, 2*heads*64] (= [k | v]).  Returns out [batches*Lq, heads*64]."""
     name = "attention"
-    dev = _check_cuda(name, q, kv)
+    dev = _check_cuda(name, q, kv, out)
     Cd = heads * 64
     if out is None:
         out = torch.empty(batches * Lq, Cd, dtype=torch.float16, device=dev)
     k0 = 0 if k_col0 is None else k_col0
     v0 = Cd if v_col0 is None else v_col0
+    _check_rows(name, q, batches * Lq, Cd, "q")
+    _check_rows(name, kv, batches * Lkv, max(k0, v0) + Cd, "kv")
+    _check_rows(name, out, batches * Lq, Cd, "out")
     with _Dev(dev):
         _lib.call("qvggt_attention", _ptr(q), q.stride(0), _ptr(kv), kv.stride(0), k0, v0, _ptr(out), out.stride(0),
                   batches, Lq, Lkv, heads, _stream(q))

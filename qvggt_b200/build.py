@@ -1,13 +1,14 @@
 """Build the sm_100a CUDA library ``libqvggt_b200.so`` in-tree.
 
-    python -m qvggt_b200.build [--debug-bounds] [-j N]
+    python -m qvggt_b200.build [-j N] [-v] [--ptxas-v]
 
 Each ``csrc/*.cu`` is compiled with nvcc for ``compute_100a``/``sm_100a``
 (``-lineinfo -O3``) into ``_build/`` and linked into
 ``qvggt_b200/libqvggt_b200.so``.  Only the CUDA runtime is linked; the driver
 entry point used for TMA descriptors is fetched at run time through
-``cudaGetDriverEntryPoint``.  Rebuilds only what changed (source or header
-newer than the object).
+``cudaGetDriverEntryPoint``.  Every call compiles every source from scratch
+(the object directory is emptied first; a full build takes well under a
+minute), so a stale object or library can never stand in for the sources.
 """
 from __future__ import annotations
 
@@ -37,16 +38,8 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _deps() -> float:
-    hdrs = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.hpp")) + \
-        glob.glob(os.path.join(ROOT, "include", "*.h"))
-    return max([os.path.getmtime(h) for h in hdrs] + [os.path.getmtime(__file__)])
-
-
 def _compile(src: str, extra: list[str], verbose: bool) -> str:
     obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
-    if os.path.exists(obj) and os.path.getmtime(obj) > max(os.path.getmtime(src), _deps()):
-        return obj
     cmd = [nvcc()] + ARCH + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
     if verbose:
         print(" ".join(cmd), flush=True)
@@ -58,16 +51,14 @@ def _compile(src: str, extra: list[str], verbose: bool) -> str:
     return obj
 
 
-def build(debug_bounds: bool = False, jobs: int = 8, verbose: bool = False, ptxas_v: bool = False) -> str:
-    os.makedirs(BUILD, exist_ok=True)
-    extra = ["-DQVGGT_DEBUG_BOUNDS"] if debug_bounds else []
-    if ptxas_v:
-        extra += ["-Xptxas", "-v"]
+def build(jobs: int = 8, verbose: bool = False, ptxas_v: bool = False) -> str:
+    if os.path.isdir(BUILD):
+        shutil.rmtree(BUILD)
+    os.makedirs(BUILD)
+    extra = ["-Xptxas", "-v"] if ptxas_v else []
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra, verbose), srcs))
-    if os.path.exists(LIB) and os.path.getmtime(LIB) > max(os.path.getmtime(o) for o in objs):
-        return LIB
     tmp = LIB + ".tmp"
     cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcudart"]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -79,9 +70,8 @@ def build(debug_bounds: bool = False, jobs: int = 8, verbose: bool = False, ptxa
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--debug-bounds", action="store_true")
     ap.add_argument("-j", type=int, default=8)
     ap.add_argument("-v", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true")
     a = ap.parse_args()
-    print(build(a.debug_bounds, a.j, a.v, a.ptxas_v))
+    print(build(a.j, a.v, a.ptxas_v))

@@ -585,13 +585,8 @@ extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, 
   }
   auto kfn = poly == 0 ? attn_fwd_kernel<0> : poly == 1 ? attn_fwd_kernel<1> : poly == 2 ? attn_fwd_kernel<2>
            : poly == 3 ? attn_fwd_kernel<3> : attn_fwd_kernel<4>;
-  static bool attr_set[64][5] = {};
-  if (di.device < 64 && !attr_set[di.device][poly]) {
-    int rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::TOTAL),
-                        "cudaFuncSetAttribute(attention)");
-    if (rc) return rc;
-    attr_set[di.device][poly] = true;
-  }
+  static DeviceFlags attr_set[5];
+  if (int rc = ensure_smem(attr_set[poly], kfn, AttnSmem::TOTAL, "cudaFuncSetAttribute(attention)")) return rc;
   kfn<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK, tmV, a);
   int rc = check_cuda(cudaGetLastError(), "attention launch");
   if (!rc) count_launch(1);

@@ -142,14 +142,8 @@ extern "C" int qvggt_attention_small(const void* q, int64_t q_stride, const void
   const long long grid = batches * heads * a.chunks;
   if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention_small: grid too large");
   const int smem = (2 * SA_MAXL * SA_ROW + SA_WARPS * 64) * 4 + SA_WARPS * SA_MAXL * 4;
-  static bool attr_set[64] = {};
-  const DeviceInfo& di = device_info();
-  if (di.device >= 0 && di.device < 64 && !attr_set[di.device]) {
-    int rc = check_cuda(cudaFuncSetAttribute(attn_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                        "cudaFuncSetAttribute(attention_small)");
-    if (rc) return rc;
-    attr_set[di.device] = true;
-  }
+  static DeviceFlags attr_set;
+  if (int rc = ensure_smem(attr_set, attn_small_kernel, smem, "cudaFuncSetAttribute(attention_small)")) return rc;
   attn_small_kernel<<<(unsigned)grid, SA_WARPS * 32, smem, static_cast<cudaStream_t>(stream)>>>(a);
   int rc = check_cuda(cudaGetLastError(), "attention_small launch");
   if (!rc) count_launch(1);

@@ -14,9 +14,24 @@ namespace {
 thread_local char g_errmsg[512] = {0};
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 std::atomic<uint64_t> g_launches{0};
-DeviceInfo g_dev[64];
-uint32_t* g_status_ptr[64] = {};
-std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+uint32_t* g_status_ptr[kMaxDevices] = {};
+std::once_flag g_status_once[kMaxDevices];
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+void query_device(DeviceInfo& d, int dev) {
+  cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+  d.device = dev;
+}
 }  // namespace
 
 // The device status word.  One per device (every device that loads the
@@ -39,34 +54,29 @@ int check_cuda(cudaError_t e, const char* what) {
 void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 const DeviceInfo& device_info() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  DeviceInfo& d = g_dev[dev];
-  if (d.device != dev) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (d.device != dev) {
-      cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
-      cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-      cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
-      cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
-      d.device = dev;
-    }
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) {   // not cached: queried on every call
+    thread_local DeviceInfo d;
+    query_device(d, dev);
+    return d;
   }
-  return d;
+  std::call_once(g_dev_once[dev], [dev] { query_device(g_dev[dev], dev); });
+  return g_dev[dev];
 }
 
+// Address of the current device's status word (the host-side name of a
+// __device__ variable is not a device address: it is looked up once per device
+// with that device current).
 static uint32_t* status_ptr() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!g_status_ptr[dev]) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_status_ptr[dev]) {
-      void* p = nullptr;
-      if (cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess) g_status_ptr[dev] = static_cast<uint32_t*>(p);
-    }
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess ? static_cast<uint32_t*>(p) : nullptr;
   }
+  std::call_once(g_status_once[dev], [dev] {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess) g_status_ptr[dev] = static_cast<uint32_t*>(p);
+  });
   return g_status_ptr[dev];
 }
 

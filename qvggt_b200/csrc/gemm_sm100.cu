@@ -350,14 +350,8 @@ int launch_gemm(const GemmLaunch& L) {
   if (g.num_tiles == 0) return QVGGT_OK;
 
   auto kfn = gemm_kernel<BN, MODE>;
-  static bool attr_set[16] = {};
-  const int dev = di.device;
-  if (dev < 16 && !attr_set[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                    "cudaFuncSetAttribute(gemm)");
-    if (rc) return rc;
-    attr_set[dev] = true;
-  }
+  static DeviceFlags attr_set;
+  if ((rc = ensure_smem(attr_set, kfn, C::SMEM, "cudaFuncSetAttribute(gemm)"))) return rc;
   const int grid = g.num_tiles < di.num_sms ? g.num_tiles : di.num_sms;
   kfn<<<grid, C::THREADS, C::SMEM, L.stream>>>(tmA, tmB, tmS, tmZ, g);
   return check_cuda(cudaGetLastError(), "gemm launch");

@@ -441,13 +441,8 @@ int launch2(const GemmLaunch& L) {
   if (g.num_tiles == 0) return QVGGT_OK;
 
   auto kfn = gemm2sm_kernel<MODE>;
-  static bool attr_set[64] = {};
-  if (di.device < 64 && !attr_set[di.device]) {
-    rc = check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                    "cudaFuncSetAttribute(gemm2sm)");
-    if (rc) return rc;
-    attr_set[di.device] = true;
-  }
+  static DeviceFlags attr_set;
+  if ((rc = ensure_smem(attr_set, kfn, C::SMEM, "cudaFuncSetAttribute(gemm2sm)"))) return rc;
   const int max_clusters = di.num_sms / 2;
   const int clusters = g.num_tiles < max_clusters ? g.num_tiles : max_clusters;
   cudaLaunchConfig_t cfg = {};

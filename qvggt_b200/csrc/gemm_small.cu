@@ -329,29 +329,24 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
 // Opts the kernel into its dynamic shared memory once per device.
 template <int MT, int MODE>
 int ensure_smem_attr() {
-  static bool attr_set[64] = {};
+  static DeviceFlags attr_set;
   const DeviceInfo& di = device_info();
   if (SCfg<MT, MODE>::SMEM > di.max_smem_optin)
     return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: %d B shared memory exceeds the device limit",
                      SCfg<MT, MODE>::SMEM);
-  if (di.device >= 0 && di.device < 64 && !attr_set[di.device]) {
-    int rc = check_cuda(cudaFuncSetAttribute(gemm_small_kernel<MT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SCfg<MT, MODE>::SMEM),
-                        "cudaFuncSetAttribute(gemm_small)");
-    if (rc) return rc;
-    attr_set[di.device] = true;
-  }
-  return QVGGT_OK;
+  return ensure_smem(attr_set, gemm_small_kernel<MT, MODE>, SCfg<MT, MODE>::SMEM, "cudaFuncSetAttribute(gemm_small)");
 }
 
 // How many clusters of `splits` CTAs of this kernel the device holds at once
-// (cached per device and cluster size).
+// (cached per device and cluster size; relaxed atomics: two threads that both
+// find an entry empty both compute the same value).
 template <int MT, int MODE>
 int active_clusters(int splits) {
-  static int cache[64][MAX_SPLITS + 1] = {};
+  static std::atomic<int> cache[kMaxDevices][MAX_SPLITS + 1];
   const DeviceInfo& di = device_info();
-  const int dev = di.device >= 0 && di.device < 64 ? di.device : 0;
-  int& c = cache[dev][splits];
+  std::atomic<int> dummy{0};
+  std::atomic<int>& slot = (di.device >= 0 && di.device < kMaxDevices) ? cache[di.device][splits] : dummy;
+  int c = slot.load(std::memory_order_relaxed);
   if (c == 0) {
     if (ensure_smem_attr<MT, MODE>()) return 0;
     cudaLaunchConfig_t cfg = {};
@@ -371,6 +366,7 @@ int active_clusters(int splits) {
       n = -1;  // unknown: treated as "does not fit"
     }
     c = n;
+    slot.store(c, std::memory_order_relaxed);
   }
   return c;
 }

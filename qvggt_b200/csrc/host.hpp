@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -23,14 +24,39 @@ void count_launch(int n);
 // Maps a CUDA error to QVGGT_ERR_CUDA with the CUDA message; 0 if success.
 int check_cuda(cudaError_t e, const char* what);
 
+constexpr int kMaxDevices = 64;
+
 struct DeviceInfo {
   int device = -1;
   int num_sms = 0;
   int max_smem_optin = 0;
   int cc_major = 0, cc_minor = 0;
 };
-// Properties of the current device (cached per device).
+// Properties of the current device, queried once per device (std::call_once,
+// so a second host thread never sees a half-filled entry).
 const DeviceInfo& device_info();
+
+// Once-per-device host set-up flags (kernel attributes).  A thread that sees a
+// device's flag set also sees the set-up published before it; two threads that
+// both find it clear both run the (idempotent) set-up.  Devices beyond
+// kMaxDevices never cache: their set-up runs on every call.
+struct DeviceFlags {
+  std::atomic<bool> done[kMaxDevices];
+  bool test(int dev) const { return dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire); }
+  void set(int dev) {
+    if (dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
+  }
+};
+
+// Raises a kernel's dynamic shared-memory limit to `bytes`, once per device.
+template <class Kernel>
+int ensure_smem(DeviceFlags& flags, Kernel kernel, int bytes, const char* what) {
+  const int dev = device_info().device;
+  if (flags.test(dev)) return QVGGT_OK;
+  const int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (rc == QVGGT_OK) flags.set(dev);
+  return rc;
+}
 
 // Device status word of the current device (library-owned; see capi.cu) and
 // the wait budget every bounded device-side wait uses.

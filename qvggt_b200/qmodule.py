@@ -105,7 +105,7 @@ class WQLinear(nn.Module):
         qscales[:, : scales.shape[1]] = scales
         awq_linear.scales = qscales.transpose(1, 0).contiguous()
         if linear.bias is not None:
-            awq_linear.bias = linear.bias.clone().to(dtype)
+            awq_linear.bias = linear.bias.detach().clone().to(dtype)
         gidx = torch.arange(linear.in_features, device=scales.device) // G
         intweight = torch.round((linear.weight.data + scale_zeros[:, gidx]) / qscales[:, gidx]).to(torch.int32)
         awq_linear.qweight = pack_intweight(intweight.contiguous(), interleave=4, kstride=64)
