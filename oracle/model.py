@@ -206,3 +206,82 @@ def block_pair_forward(tokens: torch.Tensor, frame_blk: dict, global_blk: dict,
     xf = block_forward(tokens, frame_blk, pos)
     xg = block_forward(xf.reshape(1, S * P, C), global_blk, pos.repeat(S, 1))
     return xf, xg.reshape(S, P, C)
+
+
+# --------------------------------------------------------------- DINOv2 front
+# The aggregator's patch embed is a DINOv2 ViT-L/14 with 4 register tokens,
+# kept in fp16 and unquantised (the reference excludes it from quantisation at
+# ``qvggt/inference/loader.py:346``).  Its forward, restated from the published
+# DINOv2 / VGGT models (vggt-hf is not vendored, so this is unpinned):
+#   images in [0, 1] -> (x - mean) / std (ImageNet statistics, fp16 ops)
+#   -> 14x14 stride-14 convolution (+ bias) = patch tokens
+#   -> [cls + pos[0] | 4 registers | patches + pos[1:]]
+#   -> 24 pre-LN blocks without RoPE (LayerScale, exact-erf GELU)
+#   -> final LayerNorm; the patch rows are the aggregator's patch tokens.
+
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+
+
+def patchify(images: torch.Tensor, patch: int = 14, mean=IMAGENET_MEAN, std=IMAGENET_STD) -> torch.Tensor:
+    """images fp16 [S, 3, H, W] -> normalised patches fp16 [S * (H/p) * (W/p), 3*p*p],
+    column c*p*p + ky*p + kx (the flattened conv weight's order).  The
+    normalisation rounds to fp16 after the subtraction and after the division
+    (an fp16 model's buffers and arithmetic)."""
+    S, Cin, H, W = images.shape
+    m = torch.tensor(mean, dtype=F16).float().view(1, 3, 1, 1)
+    s = torch.tensor(std, dtype=F16).float().view(1, 3, 1, 1)
+    x = r16(r16(images.float() - m).float() / s)
+    x = x.reshape(S, Cin, H // patch, patch, W // patch, patch).permute(0, 2, 4, 1, 3, 5)
+    return x.reshape(S * (H // patch) * (W // patch), Cin * patch * patch).contiguous()
+
+
+def patch_embed_forward(images: torch.Tensor, pe: dict, heads: int = 16, eps: float = 1e-6) -> torch.Tensor:
+    """DINOv2 front over images [S, 3, H, W] fp16 -> normalised tokens fp16
+    [S, 5 + n_patch, C] ([cls | 4 registers | patches] after the final LayerNorm).
+
+    ``pe`` holds: ``patch_w`` [C, 3*p*p] fp16, ``patch_b`` [C], ``cls`` [C],
+    ``registers`` [4, C], ``pos_cls`` [C], ``pos_patch`` [n_patch, C],
+    ``blocks`` (dicts for :func:`block_forward`, dense fp16 linears),
+    ``norm_w`` / ``norm_b``, ``patch``."""
+    S = images.shape[0]
+    p = pe["patch"]
+    x = patchify(images, p)
+    n = x.shape[0] // S
+    C = pe["patch_w"].shape[0]
+    lin = QLinear("f16", weight=pe["patch_w"], bias=pe["patch_b"])
+    tok = lin(x).reshape(S, n, C)
+    pos_p = torch.as_tensor(pe["pos_patch"]).float()
+    pos_c = torch.as_tensor(pe["pos_cls"]).float()
+    cls = r16(torch.as_tensor(pe["cls"]).float() + pos_c).reshape(1, 1, C).expand(S, 1, C)
+    regs = torch.as_tensor(pe["registers"]).to(F16).reshape(1, -1, C).expand(S, -1, C)
+    patches = r16(tok.float() + pos_p)
+    x = torch.cat([cls, regs, patches], dim=1).contiguous()
+    for blk in pe["blocks"]:
+        x = block_forward(x, blk, None, heads, eps)
+    return layernorm(x, pe["norm_w"], pe["norm_b"], eps)
+
+
+def aggregator_tokens(pe_out: torch.Tensor, specials: torch.Tensor, frame_offset: int = 0,
+                      patch_start: int = 5) -> torch.Tensor:
+    """[S, 5 + n, C] DINOv2 output -> aggregator input [S, 5 + n, C]: the
+    DINOv2 special rows are dropped and replaced by the aggregator's camera +
+    register tokens, set 0 for the first frame of the sequence (global frame
+    index 0) and set 1 for every other frame.  ``specials`` is [2, 5, C]."""
+    S = pe_out.shape[0]
+    sp = torch.as_tensor(specials).to(F16)
+    rows = [sp[0 if (f + frame_offset) == 0 else 1] for f in range(S)]
+    return torch.cat([torch.stack(rows), pe_out[:, patch_start:]], dim=1).contiguous()
+
+
+def aggregator_forward(images: torch.Tensor, pe: dict, specials, frame_blocks: list, global_blocks: list,
+                       patch_start: int = 5, grid_w: int = 37):
+    """The full aggregator on S frames: DINOv2 front, special tokens, then the
+    frame / global block pairs.  Returns (aggregator input tokens, last frame
+    block output, last global block output), each [S, P, C]."""
+    x = aggregator_tokens(patch_embed_forward(images, pe), specials, 0, patch_start)
+    x0 = x
+    xf = x
+    for fb, gb in zip(frame_blocks, global_blocks):
+        xf, x = block_pair_forward(x, fb, gb, patch_start, grid_w)
+    return x0, xf, x

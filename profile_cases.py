@@ -8,6 +8,7 @@
     python profile_cases.py trunk                  # camera-head trunk (4 blocks, width 2048)
     python profile_cases.py forward w4|w8 [S] [n]  # whole aggregator forward, frames/s
     python profile_cases.py time                   # CUDA-event timings of all of the above
+    python profile_cases.py sdpa                   # torch SDPA backends vs ours at the bench's attention shapes
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
 launch) on seeded synthetic data sized above the 126 MB L2 where it matters.
@@ -176,6 +177,46 @@ def forward_time(kind="w4", S=32, steps=3):
     print(f"aggregator forward {kind} S={S}: {t * 1e3:.1f} ms, {S / t:.2f} frames/s")
 
 
+def sdpa_bar(iters=5):
+    """torch's scaled_dot_product_attention (each fp16 backend this build
+    offers: cuDNN, flash, memory-efficient) against this library's kernel at
+    the benchmark's attention shapes: the global block at S = 32 on one GPU
+    (1 x 16 heads x 43,968 tokens), the frame blocks (32 x 16 x 1,374) and the
+    global block of 8-GPU ranks (Lq = 5,496 against 43,968).  CUDA events,
+    warm launches; SM clocks sampled during the timed loops."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from bench import ClockSampler
+    shapes = [("global S=32", 1, 43968, 43968), ("frame S=32", 32, 1374, 1374), ("global rank of 8", 1, 5496, 43968)]
+    backends = [("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION),
+                ("efficient", SDPBackend.EFFICIENT_ATTENTION)]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for name, b, Lq, Lkv in shapes:
+            C = 1024
+            q = torch.randn(b * Lq, C, dtype=torch.float16, device="cuda")
+            kv = torch.randn(b * Lkv, 2 * C, dtype=torch.float16, device="cuda")
+            out = torch.empty(b * Lq, C, dtype=torch.float16, device="cuda")
+            fl = 4.0 * b * Lq * Lkv * C
+            fn = lambda: eng.attention(q, kv, 16, b, Lq, Lkv, out=out)
+            fn()
+            t = _time(fn, iters)
+            row = [f"{name} (b={b}, Lq={Lq}, Lkv={Lkv}): qvggt {t * 1e3:.3f} ms {fl / t / 1e12:.0f} TFLOP/s"]
+            qh = q.view(b, Lq, 16, 64).transpose(1, 2)
+            kh = kv[:, :C].view(b, Lkv, 16, 64).transpose(1, 2)
+            vh = kv[:, C:].view(b, Lkv, 16, 64).transpose(1, 2)
+            for bname, be in backends:
+                try:
+                    with sdpa_kernel([be]):
+                        f2 = lambda: F.scaled_dot_product_attention(qh, kh, vh)
+                        f2()
+                        t2 = _time(f2, iters)
+                    row.append(f"sdpa-{bname} {t2 * 1e3:.3f} ms {fl / t2 / 1e12:.0f} TFLOP/s")
+                except RuntimeError as e:
+                    row.append(f"sdpa-{bname} unavailable ({str(e).splitlines()[0][:60]})")
+            print("  ".join(row), flush=True)
+    print("clocks during the timed loops:", clk.summary())
+
+
 def _time(fn, iters=20, graph=False):
     """Average device time per call.  graph=True captures the `iters` calls in
     one CUDA graph first, so host launch overhead does not pace short kernels."""
@@ -222,6 +263,8 @@ def main(argv):
         trunk_time()
     elif what == "forward":
         forward_time(argv[1] if len(argv) > 1 else "w4", *(int(v) for v in argv[2:4]))
+    elif what == "sdpa":
+        sdpa_bar()
     elif what == "time":
         for L, b in ((16384, 1), (43968, 1), (1374, 32)):
             fn, fl = attn(L, b)

@@ -48,7 +48,9 @@ class AggConfig:
     grid_w: int = 37
     eps: float = 1e-6
     rope_base: float = 100.0
-    qk_norm: bool = False
+    # VGGT-1B's aggregator blocks LayerNorm q and k per head (over head_dim)
+    # before RoPE; the DINOv2 front's blocks do not.
+    qk_norm: bool = True
     group_size: int = 128
     layer_scale: float = 0.01
 
@@ -313,6 +315,14 @@ class VGGTAggregator:
         self.tokens = torch.empty(frames_local, cfg.tokens_per_frame, C, dtype=F16, device=dev)
 
     def forward(self, images: torch.Tensor, keep: tuple[int, ...] = ()) -> dict:
+        """The DINOv2 front, then the frame / global pairs (which update
+        ``self.tokens`` in place); returns the runner's outputs."""
+        return self.runner.forward(self.embed(images), keep)
+
+    def embed(self, images: torch.Tensor) -> torch.Tensor:
+        """images [S_local, 3, H, W] -> the aggregator's input tokens
+        ``self.tokens`` [S_local, P, C]: DINOv2 front, final LayerNorm, then
+        camera / register tokens in place of DINOv2's special rows."""
         cfg, pe = self.cfg, self.pe
         P, C = cfg.tokens_per_frame, cfg.dim
         eng.patchify(images, pe.patch, pe.k_pad, out=self.patches)
@@ -326,7 +336,7 @@ class VGGTAggregator:
         eng.layernorm(x, pe.norm_w, pe.norm_b, cfg.eps, out=h)
         eng.assemble_tokens(h, P, cfg.patch_start, self.agg_specials, cfg.patch_start, True, None, self.tokens,
                             self.S_local, P, frame_offset=self.rank * self.S_local)
-        return self.runner.forward(self.tokens, keep)
+        return self.tokens
 
     def infer(self, images_host: torch.Tensor, out_host: torch.Tensor | None = None):
         """Public end-to-end call: host images [S_local, 3, H, W] fp16 (pinned

@@ -49,14 +49,16 @@ def random_linear(K: int, N: int, gen: torch.Generator, device, kind: str = "w4"
     return Linear("f16", bias, weight=w.to(F16).contiguous())
 
 
-def random_block(cfg: AggConfig, gen: torch.Generator, device, kind: str = "w4", layer_scale: float | None = None
-                 ) -> Block:
+def random_block(cfg: AggConfig, gen: torch.Generator, device, kind: str = "w4", layer_scale: float | None = None,
+                 qk_norm: bool | None = None) -> Block:
+    """One random-init block; ``qk_norm`` (default ``cfg.qk_norm``) adds the
+    per-head q / k LayerNorm weights."""
     C = cfg.dim
     hd = C // cfg.heads
     ls = cfg.layer_scale if layer_scale is None else layer_scale
     r = lambda *shape: torch.randn(*shape, generator=gen, device=device)
     qn = None
-    if cfg.qk_norm:
+    if cfg.qk_norm if qk_norm is None else qk_norm:
         qn = tuple(t.to(F16) for t in (1 + 0.1 * r(hd), 0.1 * r(hd), 1 + 0.1 * r(hd), 0.1 * r(hd)))
     return Block(
         norm1_w=(1 + 0.1 * r(C)).to(F16), norm1_b=(0.1 * r(C)).to(F16),
@@ -80,8 +82,10 @@ def random_aggregator_blocks(cfg: AggConfig, seed: int, device, depth: int | Non
 
 
 def random_patch_embed(cfg: AggConfig, gen: torch.Generator, device, depth: int = 24, patch: int = 14,
-                       k_pad: int = 640):
-    """Random-init DINOv2 ViT-L/14-reg4 front (fp16, unquantised), LayerScale 1e-5 as DINOv2 initialises it."""
+                       k_pad: int = 640, layer_scale: float = 1e-5):
+    """Random-init DINOv2 ViT-L/14-reg4 front (fp16, unquantised, no q/k norm),
+    LayerScale 1e-5 as DINOv2 initialises it (tests raise it so the blocks'
+    updates are not lost in the residual)."""
     from .aggregator import PatchEmbed
     C = cfg.dim
     kin = 3 * patch * patch
@@ -91,7 +95,7 @@ def random_patch_embed(cfg: AggConfig, gen: torch.Generator, device, depth: int 
     pos = torch.zeros(cfg.tokens_per_frame, C, device=device)
     pos[0] = r(C) * 0.02
     pos[cfg.patch_start:] = r(cfg.tokens_per_frame - cfg.patch_start, C) * 0.02
-    blocks = [random_block(cfg, gen, device, kind="f16", layer_scale=1e-5) for _ in range(depth)]
+    blocks = [random_block(cfg, gen, device, kind="f16", layer_scale=layer_scale, qk_norm=False) for _ in range(depth)]
     return PatchEmbed(patch_w=w.to(F16).contiguous(), patch_b=(r(C) * 0.01).to(F16),
                       specials=(r(1, cfg.patch_start, C) * 0.02).to(F16).contiguous(), pos=pos.to(F16).contiguous(),
                       blocks=blocks, norm_w=(1 + 0.1 * r(C)).to(F16), norm_b=(0.1 * r(C)).to(F16), patch=patch,
@@ -99,13 +103,13 @@ def random_patch_embed(cfg: AggConfig, gen: torch.Generator, device, depth: int 
 
 
 def random_vggt_aggregator(cfg: AggConfig, seed: int, device, frames_local: int, group=None, world: int = 1,
-                           rank: int = 0, pe_depth: int = 24, kind: str = "w4"):
+                           rank: int = 0, pe_depth: int = 24, kind: str = "w4", pe_layer_scale: float = 1e-5):
     """Full synthetic VGGT-1B aggregator: DINOv2 front in fp16 + ``cfg.depth``
     frame/global pairs with ``kind`` linears ("w4": BASELINE config 2, "w8":
     the W8A8 chain of config 3), identical on every rank."""
     from .aggregator import VGGTAggregator
     gen = torch.Generator(device=device).manual_seed(seed)
-    pe = random_patch_embed(cfg, gen, device, depth=pe_depth)
+    pe = random_patch_embed(cfg, gen, device, depth=pe_depth, layer_scale=pe_layer_scale)
     specials = (torch.randn(2, cfg.patch_start, cfg.dim, generator=gen, device=device) * 0.02).to(F16).contiguous()
     frame = [random_block(cfg, gen, device, kind) for _ in range(cfg.depth)]
     glob = [random_block(cfg, gen, device, kind) for _ in range(cfg.depth)]

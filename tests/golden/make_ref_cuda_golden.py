@@ -2,6 +2,7 @@
 
     python oracle/build_ref.py            # in the container with the reference checkout
     python tests/golden/make_ref_cuda_golden.py --out ref_cuda_golden.npz [--time]
+    python tests/golden/make_ref_cuda_golden.py --gemm-pins ref_cuda_gemm_pins.npz
 
 Runs the reference kernels (built from their own sources into oracle/_ref/ by
 oracle/build_ref.py) on inputs generated from fixed seeds (regenerated
@@ -52,6 +53,59 @@ def cases():
     c["rope"] = dict(x=rng.standard_normal((37, 2, 16, 64)).astype(np.float16),
                      freqs=(rng.random((2, 37, 32)) * 10).astype(np.float32))
     return c
+
+
+# Rows of the config-0 output kept in the pin fixture: the first full tile and
+# the ragged last one (1374 = 10 x 128 + 94).  A row of C depends only on its
+# own row of A, so the GPU test computes the whole product and compares these.
+C0_ROWS = list(range(0, 64)) + list(range(1310, 1374))
+
+
+def gemm_pin_cases():
+    """Inputs of the GEMM pins (numpy, CPU), regenerated identically by the tests.
+
+    ``eye``: A = I (M = K = 1024, N = 512), so C = deq(W)^T: every output
+    element is one dequantised weight (times 1, plus exact zeros), and the
+    reference kernel's fp16 accumulation is exact -- the fixture is the
+    reference's dequantised matrix bit for bit.  The per-group scales span
+    2^-6 .. 2^6 times the config-0 distribution so the fp16 rounding of
+    q*s + (-s*z) is exercised at every magnitude; all 16 nibble values and all
+    16 zero points occur.  M = 1024 takes the reference's ``gemm_w4a16_T2``
+    path (``gemm_cuda.cu:1206-1232``), never the M <= 32 split-K path.
+    ``c0``: BASELINE config 0 (X [1374, 1024] ~ N(0,1), W 1024 -> 4096, g128, seed 0).
+    """
+    from oracle import awq
+    c = {}
+    N, K, G = 512, 1024, 128
+    rng = np.random.default_rng(12)
+    q = rng.integers(0, 16, size=(N, K), dtype=np.int32)
+    zeros = rng.integers(0, 16, size=(N, K // G)).astype(np.float32)
+    mult = 2.0 ** rng.integers(-6, 7, size=(N, K // G))
+    scales = np.maximum(np.abs(rng.standard_normal((N, K // G))) * 0.02 * mult, 1e-4).astype(np.float16)
+    gpad = awq.calculate_zeros_width(K, G) * 8
+    st = np.zeros((gpad, N), np.float16)
+    st[: K // G] = scales.T
+    szt = np.zeros((gpad, N), np.float16)
+    szt[: K // G] = (-(scales.astype(np.float32) * zeros)).astype(np.float16).T
+    c["eye"] = dict(x=np.eye(K, dtype=np.float16), qweight=awq.pack_intweight(q), scales=st, scaled_zeros=szt)
+    lin = awq.make_quantized_linear(4096, 1024, 128, seed=0, bias=False)
+    x = np.random.default_rng(0).standard_normal((1374, 1024)).astype(np.float16)
+    c["c0"] = dict(x=x, qweight=lin["qweight"], scales=lin["scales"], scaled_zeros=lin["scaled_zeros"])
+    return c
+
+
+def generate_gemm_pins(ref, dev="cuda"):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    c = gemm_pin_cases()
+    out = {}
+    d = c["eye"]
+    out["eye_y"] = ref.gemm_forward_cuda_new(t(d["x"]), t(d["qweight"]), t(d["scales"]),
+                                             t(d["scaled_zeros"])).cpu().numpy()
+    d = c["c0"]
+    y = ref.gemm_forward_cuda_new(t(d["x"]), t(d["qweight"]), t(d["scales"]), t(d["scaled_zeros"]))
+    out["c0_rows_y"] = y[torch.tensor(C0_ROWS, device=dev)].cpu().numpy()
+    torch.cuda.synchronize()
+    return out
 
 
 def generate(ref, dev="cuda"):
@@ -148,9 +202,15 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "ref_cuda_golden.npz"))
     ap.add_argument("--time", action="store_true")
+    ap.add_argument("--gemm-pins", default=None, help="write only the GEMM pin fixture to this path")
     a = ap.parse_args()
     from oracle import build_ref
     ref = build_ref.load()
+    if a.gemm_pins:
+        out = generate_gemm_pins(ref)
+        np.savez_compressed(a.gemm_pins, **out)
+        print("wrote", a.gemm_pins, {k: v.shape for k, v in out.items()})
+        return
     out = generate(ref)
     np.savez_compressed(a.out, **out)
     print("wrote", a.out, {k: v.shape for k, v in out.items()})

@@ -104,3 +104,36 @@ def test_rope_vs_reference_kernel(gold, cases, tr):
     d = cases["rope"]
     y = eng.fused_rope_with_pos_forward_func(t(d["x"]), t(d["freqs"]), tr).cpu().contiguous().numpy()
     assert np.abs(y.astype(np.float32) - gold[f"rope_y_{int(tr)}"].astype(np.float32)).max() <= 2e-3
+
+
+# ------------------------------------------------ GEMM pins (reference kernel)
+PINS = os.path.join(HERE, "golden", "ref_cuda_gemm_pins.npz")
+
+
+@pytest.fixture(scope="module")
+def pins():
+    from tests.golden.make_ref_cuda_golden import gemm_pin_cases
+    return np.load(PINS), gemm_pin_cases()
+
+
+def test_gemm_identity_bit_exact_vs_reference_kernel(pins):
+    """A = I: both kernels return the dequantised weight matrix; ours (fp32
+    accumulation) and the reference's (fp16) are exact here, so every int4
+    unpack and fp16 fma dequantisation must agree bit for bit."""
+    from qvggt_b200 import awq_inference_engine as eng
+    gold, c = pins
+    d = c["eye"]
+    y = eng.gemm_forward_cuda_new(t(d["x"]), t(d["qweight"]), t(d["scales"]), t(d["scaled_zeros"])).cpu().numpy()
+    assert np.array_equal(y.view(np.uint16), gold["eye_y"].view(np.uint16))
+
+
+def test_gemm_config0_vs_reference_kernel(pins):
+    """BASELINE config 0 (1374 x 1024 -> 4096): within the per-linear bound of
+    the reference's fp16-accumulating kernel on the fixture's rows."""
+    from qvggt_b200 import awq_inference_engine as eng
+    from tests.golden.make_ref_cuda_golden import C0_ROWS
+    gold, c = pins
+    d = c["c0"]
+    y = eng.gemm_forward_cuda_new(t(d["x"]), t(d["qweight"]), t(d["scales"]), t(d["scaled_zeros"]))
+    got = y[torch.tensor(C0_ROWS, device=DEV)].cpu()
+    assert awq.max_abs_rel(got, torch.from_numpy(gold["c0_rows_y"].astype(np.float32))) <= 1e-2

@@ -101,3 +101,17 @@ def test_fused_rope(gold, cases, tr):
     d = cases["rope"]
     y = orope.fused_rope_with_pos(torch.from_numpy(d["x"]), torch.from_numpy(d["freqs"]), bool(tr)).numpy()
     assert np.abs(y.astype(np.float32) - gold[f"rope_y_{tr}"].astype(np.float32)).max() <= 2e-3
+
+
+def test_oracle_dequant_equals_reference_kernel_bit_for_bit():
+    """The reference's ``gemm_forward_cuda_new`` with A = I returns its
+    dequantised weight matrix; the oracle's restatement of the unpack and the
+    fp16 fma (``oracle.awq.dequantize``) must equal it bit for bit."""
+    import os
+    import numpy as np
+    from oracle import awq
+    from tests.golden.make_ref_cuda_golden import gemm_pin_cases
+    gold = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ref_cuda_gemm_pins.npz"))
+    d = gemm_pin_cases()["eye"]
+    deq = awq.dequantize(d["qweight"], d["scales"], d["scaled_zeros"], 128)      # [N, K] fp16
+    assert np.array_equal(np.ascontiguousarray(deq.T).view(np.uint16), gold["eye_y"].view(np.uint16))
