@@ -233,6 +233,56 @@ def run_reference_arm(args, ws, rank):
 
 
 # ------------------------------------------------------------------- GPU arm
+def step_breakdown(ws, model, steps, t_dev, attn_ms, wait_ms):
+    """Where a step's time goes on the slowest rank (ms per step, max over
+    ranks): global attention launches, the exposed wait for the K/V all-gather
+    (the part of it the local-keys pass did not cover), everything else; plus
+    the time of the same all-gather alone on an idle GPU."""
+    attn = max_over_ranks(sum(attn_ms) / steps, ws)
+    wait = max_over_ranks(sum(wait_ms) / steps, ws)
+    d = {"global_attention_ms": attn, "gather_wait_ms": wait,
+         "other_ms": 1000.0 * t_dev / steps - attn - wait, "global_attention_calls_per_step": len(attn_ms) // steps}
+    if ws > 1:
+        from qvggt_b200.dist import gather_kv
+        r = model.runner
+        for _ in range(3):
+            gather_kv(r.ws.kv_global, r.T, r.rank, r.group)
+        torch.cuda.synchronize()
+        barrier(ws)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            gather_kv(r.ws.kv_global, r.T, r.rank, r.group)
+        b.record()
+        torch.cuda.synchronize()
+        d["allgather_alone_ms"] = max_over_ranks(a.elapsed_time(b) / 10, ws)
+        d["allgather_bytes_per_rank"] = r.ws.kv_global.numel() * 2 * (ws - 1) // ws
+        d["overlap_kv"] = r.overlap_kv
+    return d
+
+
+def check_against_one_gpu(model, cfg, args, ws, rank, dev, img_dev, S, S_local):
+    """Correctness of the sharded run: the last pair's global-block output of
+    every rank, gathered on rank 0, against a one-GPU forward of all S frames
+    with the same seeds (relative L2)."""
+    from qvggt_b200.synthetic import random_vggt_aggregator, synthetic_images
+    gl = model.forward(img_dev)[-1][1].contiguous()
+    parts = [torch.empty_like(gl) for _ in range(ws)]
+    torch.distributed.all_gather(parts, gl)
+    torch.cuda.synchronize()
+    res = None
+    if rank == 0:
+        full = torch.cat(parts).float()
+        one = random_vggt_aggregator(cfg, seed=1234, device=dev, frames_local=S, pe_depth=args.depth)
+        ref = one.forward(synthetic_images(S, seed=0).to(dev))[-1][1].float()
+        res = {"rel_l2_vs_1gpu": float((full - ref).norm() / ref.norm()), "frames": S,
+               "what": "last pair's global-block output, all ranks gathered, vs a one-GPU forward on the same seeds"}
+        del one
+        torch.cuda.empty_cache()
+    barrier(ws)
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -292,8 +342,13 @@ def main():
     model.runner.kernel_timer = None
     launches = _lib.launch_count() - launches0
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1000.0, ws)
-    attn_ms = [a.elapsed_time(b) for a, b, _ in timer]
-    attn_flop = timer[0][2] if timer else 0.0
+    # global attention: per call, the summed duration of its launches and the
+    # exposed wait for the K/V gather (split passes only)
+    attn_ms = [sum(a.elapsed_time(b) for a, b in c["passes"]) for c in timer]
+    wait_ms = [c["wait"][0].elapsed_time(c["wait"][1]) for c in timer if "wait" in c]
+    attn_flop = timer[0]["flop"] if timer else 0.0
+    breakdown = step_breakdown(ws, model, args.steps, t_dev, attn_ms, wait_ms)
+    parity = check_against_one_gpu(model, cfg, args, ws, rank, dev, img_dev, S, S_local) if ws > 1 else None
 
     # ---- end to end through the public API (host buffers)
     for _ in range(max(1, args.warmup // 2)):
@@ -344,9 +399,12 @@ def main():
                          "traffic": ATTN_READ_PER_ROW / 3 * (Lq + 2 * Lkv) + ATTN_WRITE_PER_ROW * Lq,
                          "traffic_source": "ncu dram bytes of the same kernel at L=16384, scaled by rows",
                          "peak_source": f"{peak_kind} bf16 dense sustained",
-                         "launches_timed": len(attn_ms), "avg_launch_ms": avg_attn * 1000.0,
-                         "flop_per_launch": attn_flop},
+                         "calls_timed": len(attn_ms), "avg_call_ms": avg_attn * 1000.0,
+                         "launches_per_call": len(timer[0]["passes"]) if timer else 0,
+                         "flop_per_call": attn_flop},
             "cpu_baseline": cpu,
+            "breakdown": breakdown,
+            "parity": parity,
             "gpu_launches": int(launches),
             "clocks": clocks,
         }

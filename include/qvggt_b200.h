@@ -214,6 +214,38 @@ int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_
                     int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
                     int32_t heads, void* stream);
 
+/* qvggt_attention over a chosen subset of each batch's keys, in pieces that
+ * merge exactly (the frame-sharded global block of the aggregator: a rank
+ * attends to its own K/V rows while the all-gather of the other ranks' rows is
+ * in flight, then to those rows, and the two results are merged).
+ *
+ * Keys: rows [seg0_start, seg0_start + seg0_len) and
+ * [seg1_start, seg1_start + seg1_len) of each batch's Lkv rows (seg1_len may
+ * be 0; seg0_len > 0).
+ * splits: 1..4 CTAs share each (batch, head, 256-query block), each over a
+ * consecutive part of the keys; their results are merged on the device by the
+ * last of them to finish (no CTA waits for another).  splits > 1 needs
+ * `scratch` of qvggt_attention_scratch_bytes() bytes (16-byte aligned); its
+ * first bytes are cleared on `stream` before the launch, so calls on one
+ * stream may share it, calls that may overlap on the GPU may not.
+ * lse (fp32 [batches][heads][Lq]) holds ln(sum_k exp(q.k / 8)) of each row:
+ *   lse_mode 0: not used;  1: written;  2: `out` and `lse` hold the result of
+ *   an earlier call over other keys of the same rows, which is merged with
+ *   this call's; both are overwritten with the merged result.
+ * qvggt_attention_plan() gives the split count the library would choose for a
+ * shape on the current device (fewest waves of CTAs over its SMs) and the
+ * scratch it needs.
+ * New entry points (the reference model runs PyTorch SDPA). */
+int qvggt_attention_ex(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                       int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
+                       int64_t seg0_start, int64_t seg0_len, int64_t seg1_start, int64_t seg1_len, int32_t heads,
+                       int32_t splits, int32_t lse_mode, float* lse, void* scratch, int64_t scratch_bytes,
+                       void* stream);
+int qvggt_attention_plan(int64_t batches, int64_t Lq, int64_t keys, int32_t heads, int32_t* splits,
+                         int64_t* scratch_bytes);
+int qvggt_attention_scratch_bytes(int64_t batches, int64_t Lq, int32_t heads, int32_t splits,
+                                  int64_t* scratch_bytes);
+
 /* Attention over short sequences with head_dim 128 (the camera-head trunk:
  * 16 heads x 128 over the S <= 256 camera tokens of each batch),
  * softmax(q k^T / sqrt(128)) v on CUDA cores in fp32.  Same token-major

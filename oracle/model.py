@@ -65,6 +65,24 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, chunk: int | None = 
     return r16(torch.cat(outs, dim=-2))
 
 
+def sdpa_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """softmax(q k^T / sqrt(d)) v in fp32 and the natural log-sum-exp of each
+    row's scaled scores; q/k/v [..., L, d].  Returns (o fp32, lse fp32 [..., Lq])."""
+    d = q.shape[-1]
+    s = (q.float() @ k.float().transpose(-1, -2)) / math.sqrt(d)
+    lse = torch.logsumexp(s, dim=-1)
+    return torch.exp(s - lse[..., None]) @ v.float(), lse
+
+
+def merge_attention(parts) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact merge of attention results over disjoint key sets: parts is a list
+    of (o, lse); o = sum_i exp(lse_i - lse) o_i with lse = logsumexp_i lse_i."""
+    lses = torch.stack([p[1] for p in parts])
+    lse = torch.logsumexp(lses, dim=0)
+    o = sum(torch.exp(p[1] - lse)[..., None] * p[0].float() for p in parts)
+    return o, lse
+
+
 class QLinear:
     """One linear in the W4A16 (``kind='w4'``), dense fp16 (``'f16'``) or
     W8A8 (``'w8'``) form, holding exactly the buffers the GPU path uses."""

@@ -9,6 +9,7 @@
     python profile_cases.py forward w4|w8 [S] [n]  # whole aggregator forward, frames/s
     python profile_cases.py time                   # CUDA-event timings of all of the above
     python profile_cases.py sdpa                   # torch SDPA backends vs ours at the bench's attention shapes
+    python profile_cases.py ranks [S]              # global attention of one rank of N = 1, 2, 4, 8 (split plans)
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
 launch) on seeded synthetic data sized above the 126 MB L2 where it matters.
@@ -217,6 +218,49 @@ def sdpa_bar(iters=5):
     print("clocks during the timed loops:", clk.summary())
 
 
+def rank_shapes(S=32, iters=5):
+    """Global attention of one rank when S frames are sharded over N GPUs
+    (Lq = S/N frames of queries against all S frames of keys): one launch
+    over all keys, the same with the library's split plan, and the two-pass
+    form the aggregator uses with N > 1 (own keys with lse, then the others'
+    keys merged); TFLOP/s of the whole call."""
+    from qvggt_b200.dist import remote_segments
+    P, C, heads = 1374, 1024, 16
+    Lkv = S * P
+    kv = torch.randn(Lkv, 2 * C, dtype=torch.float16, device="cuda")
+    for N in (1, 2, 4, 8):
+        if S % N:
+            continue
+        T = S // N * P
+        q = torch.randn(T, C, dtype=torch.float16, device="cuda")
+        out = torch.empty(T, C, dtype=torch.float16, device="cuda")
+        lse = torch.empty(heads, T, dtype=torch.float32, device="cuda")
+        fl = 4.0 * T * Lkv * C
+        sp_all, nb_all = eng.attention_plan(1, T, Lkv, heads)
+        sp_loc, nb1 = eng.attention_plan(1, T, T, heads)
+        sp_rem, nb2 = eng.attention_plan(1, T, Lkv - T, heads) if N > 1 else (1, 0)
+        scratch = torch.empty(max(nb_all, nb1, nb2, 256), dtype=torch.uint8, device="cuda")
+        r = N // 2                                   # a middle rank: its remote keys are two segments at N >= 4
+
+        def two_pass():
+            eng.attention_ex(q, kv, heads, 1, T, Lkv, out=out, segments=[(r * T, T)], splits=sp_loc, lse=lse,
+                             lse_mode=1, scratch=scratch)
+            if N > 1:
+                eng.attention_ex(q, kv, heads, 1, T, Lkv, out=out, segments=remote_segments(T, N, r), splits=sp_rem,
+                                 lse=lse, lse_mode=2, scratch=scratch)
+
+        cases = [("one launch", lambda: eng.attention(q, kv, heads, 1, T, Lkv, out=out)),
+                 (f"split plan {sp_all}", lambda: eng.attention_ex(q, kv, heads, 1, T, Lkv, out=out, splits=sp_all,
+                                                                  scratch=scratch)),
+                 (f"local {sp_loc} + remote {sp_rem}", two_pass)]
+        row = [f"N={N} (Lq={T}, Lkv={Lkv}):"]
+        for name, f in cases:
+            f()
+            t = _time(f, iters)
+            row.append(f"{name} {t * 1e3:.3f} ms {fl / t / 1e12:.0f} TFLOP/s")
+        print("  ".join(row), flush=True)
+
+
 def _time(fn, iters=20, graph=False):
     """Average device time per call.  graph=True captures the `iters` calls in
     one CUDA graph first, so host launch overhead does not pace short kernels."""
@@ -265,6 +309,8 @@ def main(argv):
         forward_time(argv[1] if len(argv) > 1 else "w4", *(int(v) for v in argv[2:4]))
     elif what == "sdpa":
         sdpa_bar()
+    elif what == "ranks":
+        rank_shapes(*(int(v) for v in argv[1:2]))
     elif what == "time":
         for L, b in ((16384, 1), (43968, 1), (1374, 32)):
             fn, fl = attn(L, b)

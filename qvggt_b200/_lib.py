@@ -42,6 +42,10 @@ SIGNATURES = {
     "qvggt_rope_with_pos": [vp, vp, vp, i64, i64, i64, i64, i64, i64p, i64p, vp],
     "qvggt_qkv_rope2d": [vp, vp, vp, i64, i32, i64, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp, f32, vp],
     "qvggt_attention": [vp, i64, vp, i64, i64, i64, vp, i64, i64, i64, i64, i32, vp],
+    "qvggt_attention_ex": [vp, i64, vp, i64, i64, i64, vp, i64, i64, i64, i64, i64, i64, i64, i64, i32, i32, i32, vp,
+                           vp, i64, vp],
+    "qvggt_attention_plan": [i64, i64, i64, i32, C.POINTER(i32), i64p],
+    "qvggt_attention_scratch_bytes": [i64, i64, i32, i32, i64p],
     "qvggt_attention_small": [vp, i64, vp, i64, i64, i64, vp, i64, i64, i64, i32, vp],
     "qvggt_selftest_wait_timeout": [u64, u32p],
     "qvggt_patchify": [vp, vp, i64, i32, i32, i32, i32, C.POINTER(f32), C.POINTER(f32), vp],

@@ -20,8 +20,11 @@ Kernel sequence of one block (W4A16):
 
 Multi-GPU: frames are sharded contiguously over ranks.  Frame blocks and all
 linears are rank-local; a global block writes its roped K / V straight into
-this rank's slice of a [S*P, 2C] buffer and all-gathers it over NCCL before the
-attention of the local queries against all keys.  No other communication.
+this rank's slice of a [S*P, 2C] buffer and starts the NCCL all-gather of the
+buffer; while it is in flight the local queries attend to the rank's own keys
+(writing the rows' log-sum-exp), then, once the gather has landed, to the
+other ranks' keys, and the second pass merges the two results exactly.  No
+other communication.
 """
 from __future__ import annotations
 
@@ -32,7 +35,7 @@ import numpy as np
 import torch
 
 from . import awq_inference_engine as eng
-from .dist import gather_kv, kv_slice
+from .dist import gather_kv, kv_slice, remote_segments
 
 F16 = torch.float16
 
@@ -143,6 +146,12 @@ class Workspace:
         self.kv_global = torch.empty(T_global, 2 * C, dtype=F16, device=device)
         self.attn = torch.empty(T_local, C, dtype=F16, device=device)
         self.mlp = torch.empty(T_local, cfg.mlp_ratio * C, dtype=F16, device=device)
+        # split-pass global attention (more than one rank): per-row log-sum-exp
+        # and the kernels' split scratch
+        self.lse = None
+        self.attn_scratch = None
+        if T_global > T_local:
+            self.lse = torch.empty(cfg.heads, T_local, dtype=torch.float32, device=device)
 
 
 class AggregatorRunner:
@@ -154,7 +163,7 @@ class AggregatorRunner:
     """
 
     def __init__(self, cfg: AggConfig, frame_blocks: list[Block], global_blocks: list[Block], frames_local: int,
-                 device, group=None, world: int = 1, rank: int = 0):
+                 device, group=None, world: int = 1, rank: int = 0, overlap_kv: bool = True):
         self.cfg = cfg
         self.frame_blocks = frame_blocks
         self.global_blocks = global_blocks
@@ -168,8 +177,20 @@ class AggregatorRunner:
         self.w8a8 = any(b.qkv.kind == "w8" for b in list(frame_blocks) + list(global_blocks))
         self.ws = Workspace(self.T, self.T * world, cfg, self.device, self.w8a8)
         self.cos, self.sin = rope_tables(cfg, self.device)
-        # When a list: (start event, end event, algorithmic FLOP) of every
-        # global-attention launch is appended (CUDA events on the current stream).
+        # With more than one rank the global attention runs as a local-keys
+        # pass overlapping the K/V all-gather and a remote-keys pass
+        # (overlap_kv), or after the whole gather (overlap_kv=False).
+        self.overlap_kv = overlap_kv and world > 1
+        if self.overlap_kv:
+            with torch.cuda.device(self.device):
+                self.split_local, b1 = eng.attention_plan(1, self.T, self.T, cfg.heads)
+                self.split_remote, b2 = eng.attention_plan(1, self.T, self.T * (world - 1), cfg.heads)
+            if max(b1, b2):
+                self.ws.attn_scratch = torch.empty(max(b1, b2), dtype=torch.uint8, device=self.device)
+        # When a list: one dict per global-attention call, appended by the
+        # global blocks: CUDA events ("passes": [(start, end), ...] around
+        # each attention launch; "wait": (end of the local pass, gather landed)
+        # with the split passes) and the algorithmic FLOP of the call.
         self.kernel_timer = None
 
     # ------------------------------------------------------------------ block
@@ -200,18 +221,7 @@ class AggregatorRunner:
         eng.qkv_rope_linear(ws.h, blk.qkv, cfg.heads, self.cos, self.sin, P, cfg.patch_start, cfg.grid_w, 0,
                             q_out=ws.q, kv_out=kv_dst, qk_norm=blk.qk_norm, eps=cfg.eps)
         if glob:
-            if self.world > 1:
-                kv, Lkv = gather_kv(ws.kv_global, self.T, self.rank, self.group), self.T * self.world
-            else:
-                kv, Lkv = ws.kv_local, self.T
-            if self.kernel_timer is not None:
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev0.record()
-            eng.attention(ws.q, kv, cfg.heads, 1, self.T, Lkv, out=ws.attn)
-            if self.kernel_timer is not None:
-                ev1.record()
-                self.kernel_timer.append((ev0, ev1, 4.0 * self.T * Lkv * cfg.dim))
+            self._global_attention()
         else:
             eng.attention(ws.q, ws.kv_local, cfg.heads, self.S_local, P, P, out=ws.attn)
         blk.proj(ws.attn, residual=x, gamma=blk.ls1)
@@ -219,14 +229,50 @@ class AggregatorRunner:
         blk.fc1(ws.h, out=ws.mlp, act="gelu")
         blk.fc2(ws.mlp, residual=x, gamma=blk.ls2)
 
+    def _global_attention(self) -> None:
+        """Attention of the local queries (``ws.q``) over every frame's keys
+        into ``ws.attn``; this rank's roped K / V are in its slice of
+        ``ws.kv_global`` (world > 1) or in ``ws.kv_local``."""
+        cfg, ws, T = self.cfg, self.ws, self.T
+        timer = self.kernel_timer
+        ev = (lambda: torch.cuda.Event(enable_timing=True)) if timer is not None else None
+        if self.world == 1 or not self.overlap_kv:
+            if self.world > 1:
+                kv, Lkv = gather_kv(ws.kv_global, T, self.rank, self.group), T * self.world
+            else:
+                kv, Lkv = ws.kv_local, T
+            e = [ev(), ev()] if timer is not None else None
+            if e:
+                e[0].record()
+            eng.attention(ws.q, kv, cfg.heads, 1, T, Lkv, out=ws.attn)
+            if e:
+                e[1].record()
+                timer.append({"passes": [(e[0], e[1])], "flop": 4.0 * T * Lkv * cfg.dim})
+            return
+        Lkv = T * self.world
+        work = gather_kv(ws.kv_global, T, self.rank, self.group, async_op=True)
+        e = [ev() for _ in range(4)] if timer is not None else None
+        if e:
+            e[0].record()
+        eng.attention_ex(ws.q, ws.kv_global, cfg.heads, 1, T, Lkv, out=ws.attn, segments=[(self.rank * T, T)],
+                         splits=self.split_local, lse=ws.lse, lse_mode=1, scratch=ws.attn_scratch)
+        if e:
+            e[1].record()
+        work.wait()
+        if e:
+            e[2].record()
+        eng.attention_ex(ws.q, ws.kv_global, cfg.heads, 1, T, Lkv, out=ws.attn,
+                         segments=remote_segments(T, self.world, self.rank), splits=self.split_remote, lse=ws.lse,
+                         lse_mode=2, scratch=ws.attn_scratch)
+        if e:
+            e[3].record()
+            timer.append({"passes": [(e[0], e[1]), (e[2], e[3])], "wait": (e[1], e[2]),
+                          "flop": 4.0 * T * Lkv * cfg.dim})
+
     def _attend(self, kind: str, kv_dst: torch.Tensor) -> None:
         cfg, ws = self.cfg, self.ws
         if kind == "global":
-            if self.world > 1:
-                kv, Lkv = gather_kv(ws.kv_global, self.T, self.rank, self.group), self.T * self.world
-            else:
-                kv, Lkv = ws.kv_local, self.T
-            eng.attention(ws.q, kv, cfg.heads, 1, self.T, Lkv, out=ws.attn)
+            self._global_attention()
         else:
             eng.attention(ws.q, ws.kv_local, cfg.heads, self.S_local, cfg.tokens_per_frame, cfg.tokens_per_frame,
                           out=ws.attn)

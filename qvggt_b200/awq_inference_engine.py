@@ -25,7 +25,8 @@ __all__ = [
     "gemm_forward_cuda_new", "gemv_forward_cuda_new", "w8a8_gemm_forward_cuda",
     "w8a8_gemm_fuse_bias_forward_cuda", "invoke_quant", "rms_norm_general", "gelu_and_quant",
     "fused_rope_with_pos_forward_func", "w4a16_linear", "f16_linear", "layernorm", "qkv_rope2d",
-    "attention", "attention_small", "i8_gemm_i32", "small_linear",
+    "attention", "attention_small", "i8_gemm_i32", "small_linear", "attention_ex", "attention_plan",
+    "attention_scratch_bytes",
 ]
 
 
@@ -586,3 +587,66 @@ def attention(q, kv, heads: int, batches: int, Lq: int, Lkv: int, out=None, k_co
         _lib.call("qvggt_attention", _ptr(q), q.stride(0), _ptr(kv), kv.stride(0), k0, v0, _ptr(out), out.stride(0),
                   batches, Lq, Lkv, heads, _stream(q))
     return out
+
+
+def attention_plan(batches: int, Lq: int, keys: int, heads: int) -> tuple[int, int]:
+    """(splits, scratch bytes) the library picks for this shape on the current
+    device: the split count that runs the grid in the fewest waves of CTAs
+    over the SMs."""
+    sp = C.c_int32(0)
+    nb = C.c_int64(0)
+    _lib.call("qvggt_attention_plan", batches, Lq, keys, heads, C.byref(sp), C.byref(nb))
+    return int(sp.value), int(nb.value)
+
+
+def attention_scratch_bytes(batches: int, Lq: int, heads: int, splits: int) -> int:
+    nb = C.c_int64(0)
+    _lib.call("qvggt_attention_scratch_bytes", batches, Lq, heads, splits, C.byref(nb))
+    return int(nb.value)
+
+
+def attention_ex(q, kv, heads: int, batches: int, Lq: int, Lkv: int, out=None, k_col0: int | None = None,
+                 v_col0: int | None = None, segments=None, splits: int | None = None, lse=None, lse_mode: int = 0,
+                 scratch=None):
+    """:func:`attention` over a subset of each batch's keys, in parts that merge exactly.
+
+    ``segments``: up to two (start, length) key-row ranges per batch (default
+    all Lkv rows).  ``splits``: CTAs per (batch, head, 256-query block), each
+    over a consecutive part of the keys (None: the library's plan).  ``lse``
+    (fp32 [batches, heads, Lq]): ln(sum_k exp(q.k / 8)) per row; ``lse_mode``
+    1 writes it, 2 merges this call's result with an earlier call's (``out``
+    and ``lse``, over other keys of the same rows) and writes both.
+    ``scratch``: a uint8 CUDA tensor of at least
+    :func:`attention_scratch_bytes` bytes when splits > 1 (allocated here if
+    None).  Returns ``out``."""
+    name = "attention_ex"
+    dev = _check_cuda(name, q, kv, out, lse, scratch)
+    Cd = heads * 64
+    if out is None:
+        out = torch.empty(batches * Lq, Cd, dtype=torch.float16, device=dev)
+    k0 = 0 if k_col0 is None else k_col0
+    v0 = Cd if v_col0 is None else v_col0
+    _check_rows(name, q, batches * Lq, Cd, "q")
+    _check_rows(name, kv, batches * Lkv, max(k0, v0) + Cd, "kv")
+    _check_rows(name, out, batches * Lq, Cd, "out")
+    segs = [(0, Lkv)] if segments is None else [tuple(map(int, sg)) for sg in segments if sg[1] > 0]
+    _check_shape(name, 1 <= len(segs) <= 2, "one or two non-empty key segments")
+    (s0, n0), (s1, n1) = segs[0], (segs[1] if len(segs) > 1 else (0, 0))
+    keys = n0 + n1
+    if lse_mode:
+        _check_shape(name, lse is not None and lse.dtype == torch.float32 and lse.is_contiguous()
+                     and lse.numel() >= batches * heads * Lq, "lse must be fp32 contiguous [batches, heads, Lq]")
+    with _Dev(dev):
+        if splits is None:
+            splits, _ = attention_plan(batches, Lq, keys, heads)
+        nbytes = attention_scratch_bytes(batches, Lq, heads, splits) if splits > 1 else 0
+        if nbytes and scratch is None:
+            scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        if scratch is not None:
+            _check_shape(name, scratch.dtype == torch.uint8 and scratch.is_contiguous() and scratch.numel() >= nbytes,
+                         f"scratch must be a contiguous uint8 tensor of >= {nbytes} bytes")
+        _lib.call("qvggt_attention_ex", _ptr(q), q.stride(0), _ptr(kv), kv.stride(0), k0, v0, _ptr(out),
+                  out.stride(0), batches, Lq, Lkv, s0, n0, s1, n1, heads, splits, lse_mode, _ptr(lse), _ptr(scratch),
+                  scratch.numel() if scratch is not None else 0, _stream(q))
+    return out
+

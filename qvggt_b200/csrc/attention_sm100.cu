@@ -20,11 +20,25 @@
 // more than 2^8 (then O_i and the row sum are rescaled in place); P <= 256 fits
 // fp16 and the final O / l is exact either way.
 //
+// Keys of a batch come from up to two row segments of the K/V buffer (a rank
+// of a frame-sharded global block attends first to its own rows, then to the
+// rows before and after them once the all-gather has landed), walked as one
+// sequence of 128-key tiles; a tile that ends past its segment is masked.
+// Split-KV: a (batch, head, query block) item may be cut into `splits` CTAs
+// over consecutive ranges of that tile sequence (the grid then fills the
+// 148 SMs in whole waves when the query blocks alone would leave a partial
+// wave).  Each such CTA writes its normalised rows and their log-sum-exp to
+// scratch, and the last of them to finish (a device-scope counter; no CTA
+// ever waits for another) merges all of them.  lse_mode 1 also writes the
+// log-sum-exp of every row; lse_mode 2 merges the result with an earlier call's
+// (O in `out`, log-sum-exp in `lse`) over disjoint keys.
+//
 // TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 //               O0 [384,448) O1 [448,512).
 // Warps: 0 TMA producer of Q and K, 2 TMA producer of V, 1 TMEM owner + S
 // MMA issuer, 3 PV MMA issuer, 4..7 softmax WG 0, 8..11 softmax WG 1.  All waits are bounded
 // (common.cuh).
+#include <algorithm>
 #include <cstdlib>
 
 #include "host.hpp"
@@ -33,6 +47,7 @@ namespace qv {
 namespace {
 
 constexpr int KV_STAGES = 3;
+constexpr int MAX_SPLITS = 4;          // KV splits per (batch, head, query block)
 constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 64 fp16
 constexpr int THREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
@@ -49,18 +64,43 @@ struct AttnSmem {
   // o_done[2], drain (S issuer), drain2 (PV issuer)
   static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 2;
   static constexpr int MISC = BAR + NUM_BARS * 8;
-  // MISC: +0 TMEM base, +4 abort flag, +8 status word pointer, +16 timeout (ns)
-  static constexpr int TOTAL = MISC + 24 + 1024;
+  // MISC: +0 TMEM base, +4 abort flag, +8 status word pointer, +16 timeout (ns),
+  // +24 "this CTA merges the splits" flag, +28 first key tile of this CTA
+  static constexpr int TOTAL = MISC + 32 + 1024;
 };
 
 struct AttnArgs {
-  int heads, nqb, nkv;
+  int batches, heads, nqb;
+  int splits;                      // CTAs per (batch, head, query block)
+  int nt0, nt;                     // 128-key tiles in segment 0, in both segments
+  int seg0_start, seg0_len;        // key rows within a batch
+  int seg1_start, seg1_len;        // (seg1_len 0: one segment)
+  int lse_mode;                    // 0 none, 1 write lse, 2 merge with (out, lse) of an earlier call, write lse
   long long Lq, Lkv;
   __half* out;
   long long o_stride;
+  float* lse;                      // [batches][heads][Lq], natural log of sum_k exp(q.k * scale)
+  float* part_o;                   // [splits][batches * Lq][heads * 64]   (splits > 1)
+  float* part_lse;                 // [splits][batches][heads][Lq]         (splits > 1)
+  uint32_t* counters;              // [batches * heads * nqb], zero at launch (splits > 1)
   float scale_log2;
   Ctl ctl;
 };
+
+// First key row (within the batch) and number of valid keys of tile t of the
+// two-segment key sequence.
+__device__ __forceinline__ int tile_row(const AttnArgs& a, int t) {
+  return t < a.nt0 ? a.seg0_start + t * 128 : a.seg1_start + (t - a.nt0) * 128;
+}
+__device__ __forceinline__ int tile_valid(const AttnArgs& a, int t) {
+  const int rem = t < a.nt0 ? a.seg0_len - t * 128 : a.seg1_len - (t - a.nt0) * 128;
+  return rem < 128 ? rem : 128;
+}
+// Tile range [t0, t1) of split `sp`.
+__device__ __forceinline__ void split_range(const AttnArgs& a, int sp, int& t0, int& t1) {
+  t0 = (int)((long long)sp * a.nt / a.splits);
+  t1 = (int)((long long)(sp + 1) * a.nt / a.splits);
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -105,6 +145,19 @@ __device__ __forceinline__ bool wait(const uint64_t* bar, uint32_t parity, uint3
 // lanes wait; the warp proceeds only if all saw the phase complete.
 __device__ __forceinline__ bool softmax_wait(uint32_t bar, uint32_t parity, uint32_t misc) {
   return __all_sync(0xffffffffu, wait(bar, parity, misc, ST_TIMEOUT_SOFTMAX));
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Named barrier `id` over `count` threads (whole warps).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void arrive(uint32_t bar) {
@@ -243,7 +296,11 @@ __device__ __forceinline__ float exp_store(uint32_t (&s)[128], float c, float ne
   return l0 + l1;
 }
 
-template <int POLY>
+// GENERAL = false: one split, no log-sum-exp (every single-GPU launch); its
+// epilogue only normalises and stores O.  GENERAL = true adds the split
+// merge and the log-sum-exp modes (their epilogue costs registers the plain
+// launch should not pay for).
+template <int POLY, bool GENERAL>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
@@ -267,12 +324,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + AttnSmem::MISC + 4);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int qb = blockIdx.x % a.nqb;
-  const int h = (blockIdx.x / a.nqb) % a.heads;
-  const int b = blockIdx.x / (a.nqb * a.heads);
+  const int sp = blockIdx.x % a.splits;          // KV split of this CTA
+  const int item = blockIdx.x / a.splits;        // (batch, head, query block)
+  const int qb = item % a.nqb;
+  const int h = (item / a.nqb) % a.heads;
+  const int b = item / (a.nqb * a.heads);
   const long long q_row0 = (long long)b * a.Lq + (long long)qb * 256;   // first query row of this CTA
   const long long kv_row0 = (long long)b * a.Lkv;
-  const int nkv = a.nkv;
+  int t_first, t_end;
+  split_range(a, sp, t_first, t_end);
+  const int nkv = t_end - t_first;               // KV tiles of this CTA
   // Q tiles of this CTA that hold rows of its batch (the last block of a
   // batch may end inside tile 0, e.g. 1374 = 5 x 256 + 94): an empty tile 1
   // gets no MMAs and no softmax.
@@ -297,6 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     *abort_flag = 0;
     *reinterpret_cast<uint32_t**>(smem + AttnSmem::MISC + 8) = a.ctl.status;
     *reinterpret_cast<unsigned long long*>(smem + AttnSmem::MISC + 16) = a.ctl.timeout_ns;
+    *reinterpret_cast<int*>(smem + AttnSmem::MISC + 28) = t_first;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -315,13 +377,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t misc = smem_u32(smem + AttnSmem::MISC);
 
   // Registers: launched at 168 per thread (384 x 168 = 64512); warpgroup 0
-  // (producer, MMA, two idle warps) gives back to 56, the two softmax
-  // warpgroups take 216 each: 128*56 + 256*216 = 62464 <= 64512.
+  // (producers, MMA issuers, which walk the two-segment tile sequence) gives
+  // back to 64, the two softmax warpgroups take 216 each:
+  // 128*64 + 256*216 = 63488 <= 64512.
   // setmaxnreg is warpgroup-collective: all four warps of a warpgroup must
   // execute the same one (a warpgroup whose warps disagree never completes
   // it, and the other warpgroups' increments then wait forever).
   if (warp < 4) {
-    regs_dec<56>();
+    regs_dec<64>();
     if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------ TMA producers (K + Q / V)
     if (lane == 0) {
@@ -340,7 +403,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int st = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
         if (!wait(&empty[st], ph ^ 1, misc, ST_TIMEOUT_TMA_EMPTY)) break;
-        const int row = (int)(kv_row0 + (long long)j * 128);
+        const int row = (int)(kv_row0 + tile_row(a, t_first + j));
         mbar_arrive_expect_tx(&full[st], TILE_BYTES);
         tma_load_3d(base + st * TILE_BYTES, tm, &full[st], 0, h, row);
       }
@@ -426,8 +489,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float c = a.scale_log2;
     const uint32_t bar_s_full = smem_u32(&s_full[i]);
     const uint32_t bar_s_free = bar_s_full + 16, bar_p_full = bar_s_full + 32, bar_o_done = bar_s_full + 48;
-    // keys in the last KV tile (the others are full)
-    const int last_valid = (int)(a.Lkv - (long long)(nkv - 1) * 128);
     float m_used = -INFINITY, l = 0.f;
     bool ok = i < nqt;
     for (int j = 0; ok && j < nkv; ++j) {
@@ -440,7 +501,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) arrive(bar_s_free);
 
-      const int valid = j + 1 < nkv ? 128 : last_valid;
+      // the CTA's first tile is re-read from shared memory (a register
+      // held through the loop pushed parts of the score row to local memory)
+      int tf;
+      asm volatile("ld.shared.s32 %0, [%1 + 28];" : "=r"(tf) : "r"(misc));
+      const int valid = tile_valid(a, tf + j);
       const float mx = (valid == 128) ? row_max<false>(s, valid) : row_max<true>(s, valid);
       const float m_new = fmaxf(m_used, mx * c);
       const bool need = m_new > m_used + 8.0f;
@@ -478,19 +543,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) arrive(bar_p_full);
     }
+    // ------------------------------------------------------------ epilogue
+    // `have`: O_i of the last tile is complete (warp-uniform, so the
+    // warp-collective TMEM loads below run in whole warps).
+    bool have = false;
     if (ok && nkv > 0) {
-      if (softmax_wait(bar_o_done, (nkv - 1) & 1, misc)) {
-        tc_fence_after();
-        // the CTA's coordinates are re-derived here (a volatile read of
-        // %ctaid.x) rather than kept in registers through the loop
-        uint32_t cta;
-        asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(cta));
-        const int qb_e = (int)(cta % (uint32_t)a.nqb);
-        const int h_e = (int)((cta / (uint32_t)a.nqb) % (uint32_t)a.heads);
-        const long long b_e = cta / ((uint32_t)a.nqb * (uint32_t)a.heads);
-        const long long qr = (long long)qb_e * 256 + i * 128 + r;   // row within the batch
+      have = softmax_wait(bar_o_done, (nkv - 1) & 1, misc);
+      if (have) tc_fence_after();
+    }
+    // the CTA's coordinates are re-derived here (a volatile read of
+    // %ctaid.x) rather than kept in registers through the loop
+    uint32_t cta;
+    asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(cta));
+    const uint32_t sp_e = cta % (uint32_t)a.splits;
+    const uint32_t item_e = cta / (uint32_t)a.splits;
+    const int qb_e = (int)(item_e % (uint32_t)a.nqb);
+    const int h_e = (int)((item_e / (uint32_t)a.nqb) % (uint32_t)a.heads);
+    const long long b_e = item_e / ((uint32_t)a.nqb * (uint32_t)a.heads);
+    const long long qr = (long long)qb_e * 256 + i * 128 + r;   // row within the batch
+    __half* dst = a.out + (b_e * a.Lq + qr) * a.o_stride + h_e * 64;
+    if (!GENERAL) {
+      if (have) {
         const float inv = 1.f / l;
-        __half* dst = a.out + (b_e * a.Lq + qr) * a.o_stride + h_e * 64;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t v[16];
@@ -506,6 +580,133 @@ __global__ void __launch_bounds__(THREADS, 1)
             d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
           }
         }
+      }
+    } else {
+      const bool row_ok = have && qr < a.Lq;
+      // log2 of this CTA's sum over its keys of exp2(s * c) for the row
+      const float lse2_own = m_used + log2f(l);
+      const long long bhq = ((long long)b_e * a.heads + h_e) * a.Lq + qr;        // [b][h][row]
+      const long long split_rows = (long long)a.batches * a.heads * a.Lq;       // rows of one split's parts
+      bool merge = true;
+      if (a.splits > 1) {
+        // every split parks its normalised rows; the last to finish merges
+        const long long part = (long long)sp_e * split_rows + bhq;
+        if (have) {
+          const float inv = 1.f / l;
+          float4* po = reinterpret_cast<float4*>(a.part_o + part * 64);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t v[16];
+            tmem_ld16(tO + cc * 16, v);
+            tmem_ld_wait();
+            if (row_ok) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                po[cc * 4 + e] = make_float4(__uint_as_float(v[4 * e]) * inv, __uint_as_float(v[4 * e + 1]) * inv,
+                                             __uint_as_float(v[4 * e + 2]) * inv,
+                                             __uint_as_float(v[4 * e + 3]) * inv);
+            }
+          }
+          if (row_ok) a.part_lse[part] = lse2_own;
+        }
+        fence_acq_rel_gpu();
+        named_bar_sync(1, 256);
+        if (threadIdx.x == 4 * 32) {   // the first softmax thread counts the CTA in
+          const uint32_t old = atom_add_acq_rel_gpu(a.counters + item_e, 1u);
+          const uint32_t last = old == (uint32_t)a.splits - 1u;
+          asm volatile("st.shared.u32 [%0 + 24], %1;" ::"r"(misc), "r"(last) : "memory");
+        }
+        named_bar_sync(1, 256);
+        uint32_t last;
+        asm volatile("ld.shared.u32 %0, [%1 + 24];" : "=r"(last) : "r"(misc) : "memory");
+        merge = last != 0;
+        if (merge) fence_acq_rel_gpu();
+      }
+      if (merge && have) {
+        // Weights of every part of the row from their log2-sum-exps: with
+        // splits, every split's parked part (this CTA's included, so the sum
+        // runs in split order whichever CTA merges and results repeat bit for
+        // bit); with one split, this CTA's O from TMEM; for lse_mode 2 the
+        // earlier call's result last.  The row is merged 16 columns at a time.
+        const bool own_tmem = a.splits == 1;
+        float w_part[MAX_SPLITS];
+        float lmax = own_tmem ? lse2_own : -INFINITY;
+#pragma unroll
+        for (int s2 = 0; s2 < MAX_SPLITS; ++s2) {
+          w_part[s2] = -INFINITY;
+          if (row_ok && !own_tmem && s2 < a.splits) {
+            w_part[s2] = a.part_lse[(long long)s2 * split_rows + bhq];
+            lmax = fmaxf(lmax, w_part[s2]);
+          }
+        }
+        float w_prev = -INFINITY;
+        if (row_ok && a.lse_mode == 2) {
+          w_prev = a.lse[bhq] * 1.4426950408889634f;
+          lmax = fmaxf(lmax, w_prev);
+        }
+        const float w_own = own_tmem ? ex2(lse2_own - lmax) : 0.f;
+        float wsum = w_own;
+#pragma unroll
+        for (int s2 = 0; s2 < MAX_SPLITS; ++s2) {
+          w_part[s2] = ex2(w_part[s2] - lmax);      // exp2(-inf) = 0 for absent parts
+          wsum += w_part[s2];
+        }
+        w_prev = ex2(w_prev - lmax);
+        wsum += w_prev;
+        const float inv = 1.f / wsum;
+        const float scale_own = w_own * inv / l;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float acc[16];
+          if (own_tmem) {
+            uint32_t v[16];
+            tmem_ld16(tO + cc * 16, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[e] = __uint_as_float(v[e]) * scale_own;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int s2 = 0; s2 < MAX_SPLITS; ++s2) {
+              if (own_tmem || s2 >= a.splits) continue;
+              const float w = w_part[s2] * inv;
+              const float4* po = reinterpret_cast<const float4*>(a.part_o + ((long long)s2 * split_rows + bhq) * 64 +
+                                                                 cc * 16);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float4 x = po[e];
+                acc[4 * e] += w * x.x;
+                acc[4 * e + 1] += w * x.y;
+                acc[4 * e + 2] += w * x.z;
+                acc[4 * e + 3] += w * x.w;
+              }
+            }
+            if (a.lse_mode == 2) {
+              const float w = w_prev * inv;
+              const uint4* pv = reinterpret_cast<const uint4*>(dst + cc * 16);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint4 u = pv[e];
+                const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float2 f = unpack_half2(uu[k]);
+                  acc[8 * e + 2 * k] += w * f.x;
+                  acc[8 * e + 2 * k + 1] += w * f.y;
+                }
+              }
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 16);
+            d4[0] = make_uint4(pack_half2(acc[0], acc[1]), pack_half2(acc[2], acc[3]), pack_half2(acc[4], acc[5]),
+                               pack_half2(acc[6], acc[7]));
+            d4[1] = make_uint4(pack_half2(acc[8], acc[9]), pack_half2(acc[10], acc[11]),
+                               pack_half2(acc[12], acc[13]), pack_half2(acc[14], acc[15]));
+          }
+        }
+        if (row_ok && a.lse_mode != 0) a.lse[bhq] = (lmax + log2f(wsum)) * 0.6931471805599453f;
       }
     }
   }
@@ -523,22 +724,89 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 using namespace qv;
 
-extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
-                               int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
-                               int32_t heads, void* stream) {
+namespace qv {
+namespace {
+
+inline long long align256(long long x) { return (x + 255) & ~255LL; }
+
+// Split count for `items` (batch, head, query block) items of `nt` key tiles
+// each on `slots` concurrent CTAs (one per SM): the grid runs in
+// ceil(items * s / slots) waves of CTAs that walk nt / s tiles plus a fixed
+// cost (prologue, epilogue, split merge) of about two tiles; s is the
+// cheapest of 1..MAX_SPLITS that keeps at least 8 tiles per split, taken only
+// when it beats one split by more than 3 %.
+int plan_splits(long long items, int nt, int slots) {
+  if (slots <= 0 || items <= 0) return 1;
+  auto cost = [&](int s) {
+    const long long waves = (items * s + slots - 1) / slots;
+    return (double)waves * ((double)nt / s + 2.0 * (s > 1 ? 1.5 : 1.0));
+  };
+  int best = 1;
+  double best_cost = cost(1);
+  for (int s = 2; s <= MAX_SPLITS && nt / s >= 8; ++s) {
+    const double c = cost(s);
+    if (c < best_cost * 0.97) {
+      best = s;
+      best_cost = c;
+    }
+  }
+  return best;
+}
+
+struct ScratchLayout {
+  long long counters, part_lse, part_o, total;   // byte offsets and size
+};
+
+ScratchLayout scratch_layout(long long batches, long long Lq, int heads, int splits) {
+  ScratchLayout L{};
+  if (splits <= 1) return L;
+  const long long nqb = (Lq + 255) / 256;
+  const long long rows = batches * heads * Lq;
+  L.counters = 0;
+  L.part_lse = align256(batches * heads * nqb * 4);
+  L.part_o = L.part_lse + align256((long long)splits * rows * 4);
+  L.total = L.part_o + (long long)splits * rows * 64 * 4;
+  return L;
+}
+
+}  // namespace
+
+// The launch behind every attention entry point: validates the arguments,
+// encodes the TMA maps and launches one CTA per (batch, head, query block,
+// split).  With splits > 1 the counters at the start of `scratch` are cleared
+// on the stream first.
+int attention_launch(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                     int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
+                     int64_t seg0_start, int64_t seg0_len, int64_t seg1_start, int64_t seg1_len, int32_t heads,
+                     int32_t splits, int32_t lse_mode, float* lse, void* scratch, int64_t scratch_bytes,
+                     void* stream) {
   if (batches < 0 || Lq < 0 || heads <= 0) return set_error(QVGGT_ERR_INVALID, "attention: bad shape");
   if (Lkv <= 0) return set_error(QVGGT_ERR_INVALID, "attention: Lkv must be > 0");
+  if (seg0_start < 0 || seg0_len <= 0 || seg1_start < 0 || seg1_len < 0 || seg0_start + seg0_len > Lkv ||
+      seg1_start + seg1_len > Lkv)
+    return set_error(QVGGT_ERR_INVALID, "attention: key segments must lie inside [0, Lkv) and segment 0 be non-empty");
+  if (lse_mode < 0 || lse_mode > 2) return set_error(QVGGT_ERR_INVALID, "attention: lse_mode must be 0, 1 or 2");
+  if (lse_mode != 0 && lse == nullptr) return set_error(QVGGT_ERR_INVALID, "attention: lse_mode needs an lse buffer");
   if (q_stride % 8 || kv_stride % 8 || o_stride % 8 || k_col0 % 8 || v_col0 % 8)
     return set_error(QVGGT_ERR_ALIGN, "attention: strides and column offsets must be multiples of 8");
-  if (!aligned16(q) || !aligned16(kv) || !aligned16(out))
-    return set_error(QVGGT_ERR_ALIGN, "attention: tensors must be 16-byte aligned");
+  if (!aligned16(q) || !aligned16(kv) || !aligned16(out) || (scratch && !aligned16(scratch)) ||
+      (reinterpret_cast<uintptr_t>(lse) & 3))
+    return set_error(QVGGT_ERR_ALIGN, "attention: tensors must be 16-byte aligned (lse 4-byte)");
   if (q_stride < heads * 64 || o_stride < heads * 64 || kv_stride < k_col0 + heads * 64 ||
       kv_stride < v_col0 + heads * 64)
     return set_error(QVGGT_ERR_INVALID, "attention: strides too small for the heads");
   const long long q_rows = batches * Lq, kv_rows = batches * Lkv;
-  if (q_rows + 256 > 2147483647LL || kv_rows > 2147483647LL)
+  if (q_rows + 256 > 2147483647LL || kv_rows + 128 > 2147483647LL)
     return set_error(QVGGT_ERR_UNSUPPORTED, "attention: too many rows for 32-bit TMA coordinates");
+  const long long nt0 = (seg0_len + 127) / 128, nt = nt0 + (seg1_len + 127) / 128;
+  if (splits < 1 || splits > MAX_SPLITS || splits > nt)
+    return set_error(QVGGT_ERR_INVALID, "attention: splits must be in 1..%d and at most the %lld key tiles", MAX_SPLITS,
+                     nt);
   if (batches == 0 || Lq == 0) return QVGGT_OK;
+  const ScratchLayout SL = scratch_layout(batches, Lq, heads, splits);
+  if (splits > 1 && (scratch == nullptr || scratch_bytes < SL.total))
+    return set_error(QVGGT_ERR_INVALID, "attention: %d splits need %lld bytes of scratch, got %lld", splits,
+                     SL.total, (long long)scratch_bytes);
   const DeviceInfo& di = device_info();
   if (AttnSmem::TOTAL > di.max_smem_optin)
     return set_error(QVGGT_ERR_UNSUPPORTED, "attention: shared memory %d > %d", AttnSmem::TOTAL, di.max_smem_optin);
@@ -563,32 +831,99 @@ extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, 
     if (rc) return rc;
   }
   AttnArgs a;
+  a.batches = (int)batches;
   a.heads = heads;
   a.nqb = (int)((Lq + 255) / 256);
-  a.nkv = (int)((Lkv + 127) / 128);
+  a.splits = splits;
+  a.nt0 = (int)nt0;
+  a.nt = (int)nt;
+  a.seg0_start = (int)seg0_start;
+  a.seg0_len = (int)seg0_len;
+  a.seg1_start = (int)seg1_start;
+  a.seg1_len = (int)seg1_len;
+  a.lse_mode = lse_mode;
   a.Lq = Lq;
   a.Lkv = Lkv;
   a.out = static_cast<__half*>(out);
   a.o_stride = o_stride;
+  a.lse = lse;
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  a.counters = splits > 1 ? reinterpret_cast<uint32_t*>(sc + SL.counters) : nullptr;
+  a.part_lse = splits > 1 ? reinterpret_cast<float*>(sc + SL.part_lse) : nullptr;
+  a.part_o = splits > 1 ? reinterpret_cast<float*>(sc + SL.part_o) : nullptr;
   a.scale_log2 = 0.125f * 1.4426950408889634f;
   a.ctl = make_ctl();
-  const long long grid = (long long)a.nqb * heads * batches;
+  const long long grid = (long long)a.nqb * heads * batches * splits;
   if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
   // Share of exponentials computed on the FMA pipe (pairs per 8).  Measured
   // on B200 with the split S / PV issuers: 1 is fastest at the aggregator's
   // L = 43,968 (811 TFLOP/s vs 780 for 0 and 800 for 2); the QVGGT_ATTN_POLY
   // environment variable (0..4) overrides the default.
-  static int poly = -1;
-  if (poly < 0) {
+  static const int poly = [] {
     const char* e = getenv("QVGGT_ATTN_POLY");
-    poly = (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 1;
+    return (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 1;
+  }();
+  const bool general = splits > 1 || lse_mode != 0;
+  using Kfn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AttnArgs);
+  static const Kfn plain_fns[5] = {attn_fwd_kernel<0, false>, attn_fwd_kernel<1, false>, attn_fwd_kernel<2, false>,
+                                   attn_fwd_kernel<3, false>, attn_fwd_kernel<4, false>};
+  static const Kfn general_fns[5] = {attn_fwd_kernel<0, true>, attn_fwd_kernel<1, true>, attn_fwd_kernel<2, true>,
+                                     attn_fwd_kernel<3, true>, attn_fwd_kernel<4, true>};
+  const Kfn kfn = general ? general_fns[poly] : plain_fns[poly];
+  static DeviceFlags attr_set[2][5];
+  if (int rc = ensure_smem(attr_set[general][poly], kfn, AttnSmem::TOTAL, "cudaFuncSetAttribute(attention)"))
+    return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (splits > 1) {
+    if (int rc = check_cuda(cudaMemsetAsync(a.counters, 0, (size_t)a.nqb * heads * batches * 4, st),
+                            "attention: clearing the split counters"))
+      return rc;
   }
-  auto kfn = poly == 0 ? attn_fwd_kernel<0> : poly == 1 ? attn_fwd_kernel<1> : poly == 2 ? attn_fwd_kernel<2>
-           : poly == 3 ? attn_fwd_kernel<3> : attn_fwd_kernel<4>;
-  static DeviceFlags attr_set[5];
-  if (int rc = ensure_smem(attr_set[poly], kfn, AttnSmem::TOTAL, "cudaFuncSetAttribute(attention)")) return rc;
-  kfn<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK, tmV, a);
+  kfn<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, st>>>(tmQ, tmK, tmV, a);
   int rc = check_cuda(cudaGetLastError(), "attention launch");
   if (!rc) count_launch(1);
   return rc;
+}
+
+}  // namespace qv
+
+using namespace qv;
+
+extern "C" int qvggt_attention(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                               int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq, int64_t Lkv,
+                               int32_t heads, void* stream) {
+  return attention_launch(q, q_stride, kv, kv_stride, k_col0, v_col0, out, o_stride, batches, Lq, Lkv, 0, Lkv, 0, 0,
+                          heads, 1, 0, nullptr, nullptr, 0, stream);
+}
+
+extern "C" int qvggt_attention_ex(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride, int64_t k_col0,
+                                  int64_t v_col0, void* out, int64_t o_stride, int64_t batches, int64_t Lq,
+                                  int64_t Lkv, int64_t seg0_start, int64_t seg0_len, int64_t seg1_start,
+                                  int64_t seg1_len, int32_t heads, int32_t splits, int32_t lse_mode, float* lse,
+                                  void* scratch, int64_t scratch_bytes, void* stream) {
+  return attention_launch(q, q_stride, kv, kv_stride, k_col0, v_col0, out, o_stride, batches, Lq, Lkv, seg0_start,
+                          seg0_len, seg1_start, seg1_len, heads, splits, lse_mode, lse, scratch, scratch_bytes,
+                          stream);
+}
+
+extern "C" int qvggt_attention_plan(int64_t batches, int64_t Lq, int64_t keys, int32_t heads, int32_t* splits,
+                                    int64_t* scratch_bytes) {
+  if (batches < 0 || Lq < 0 || keys <= 0 || heads <= 0 || !splits || !scratch_bytes)
+    return set_error(QVGGT_ERR_INVALID, "attention_plan: bad arguments");
+  const long long items = batches * heads * ((Lq + 255) / 256);
+  const int nt = (int)std::min<long long>((keys + 127) / 128, 1 << 30);
+  const int s = plan_splits(items, nt, device_info().num_sms);
+  *splits = s;
+  *scratch_bytes = scratch_layout(batches, Lq, heads, s).total;
+  return QVGGT_OK;
+}
+
+extern "C" int qvggt_attention_scratch_bytes(int64_t batches, int64_t Lq, int32_t heads, int32_t splits,
+                                             int64_t* scratch_bytes) {
+  if (splits < 1 || splits > MAX_SPLITS)
+    return set_error(QVGGT_ERR_INVALID, "attention_scratch_bytes: splits must be in 1..%d", MAX_SPLITS);
+  if (batches < 0 || Lq < 0 || heads <= 0 || !scratch_bytes)
+    return set_error(QVGGT_ERR_INVALID, "attention_scratch_bytes: bad arguments");
+  *scratch_bytes = scratch_layout(batches, Lq, heads, splits).total;
+  return QVGGT_OK;
 }

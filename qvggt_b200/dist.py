@@ -29,10 +29,23 @@ def kv_slice(kv_global: torch.Tensor, rows_local: int, rank: int) -> torch.Tenso
     return kv_global[rank * rows_local:(rank + 1) * rows_local]
 
 
-def gather_kv(kv_global: torch.Tensor, rows_local: int, rank: int, group=None) -> torch.Tensor:
-    """All-gather every rank's K/V rows into ``kv_global`` in place; returns it."""
-    dist.all_gather_into_tensor(kv_global, kv_slice(kv_global, rows_local, rank), group=group)
-    return kv_global
+def gather_kv(kv_global: torch.Tensor, rows_local: int, rank: int, group=None, async_op: bool = False):
+    """All-gather every rank's K/V rows into ``kv_global`` in place.  Returns
+    ``kv_global``, or with ``async_op`` the collective's work handle (its
+    ``wait()`` makes the current stream wait for the gather)."""
+    work = dist.all_gather_into_tensor(kv_global, kv_slice(kv_global, rows_local, rank), group=group,
+                                       async_op=async_op)
+    return work if async_op else kv_global
+
+
+def remote_segments(rows_local: int, world: int, rank: int) -> list[tuple[int, int]]:
+    """The other ranks' rows of the gathered K/V buffer as (start, length)
+    ranges: the rows before this rank's slice and the rows after it (empty
+    ranges dropped).  A rank attends to its own slice while the all-gather is
+    in flight, then to these rows."""
+    before = (0, rank * rows_local)
+    after = ((rank + 1) * rows_local, (world - 1 - rank) * rows_local)
+    return [sg for sg in (before, after) if sg[1] > 0]
 
 
 def special_token_set(global_frame: int) -> int:

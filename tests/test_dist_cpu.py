@@ -118,3 +118,56 @@ def test_frame_shard_rules():
         qd.frame_shard(30, 8, 0)
     kv = torch.arange(12).reshape(6, 2)
     assert torch.equal(qd.kv_slice(kv, 2, 1), kv[2:4])
+
+
+def _split_pass_worker(rank, world, port, q):
+    """The GPU runner's split-pass global attention, restated with the oracle:
+    local keys while the all-gather is in flight, then the other ranks' keys
+    (``qvggt_b200.dist.remote_segments``), merged through the log-sum-exp."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        T, heads, d = 37, 2, 16
+        g = torch.Generator().manual_seed(100 + rank)
+        ql = torch.randn(heads, T, d, generator=g)
+        kv_local = torch.randn(T, 2 * heads * d, generator=g).half()
+        kv_global = torch.empty(T * world, 2 * heads * d, dtype=torch.float16)
+        qd.kv_slice(kv_global, T, rank).copy_(kv_local)
+        work = qd.gather_kv(kv_global, T, rank, async_op=True)
+
+        def heads_of(rows):
+            k = rows[:, :heads * d].reshape(-1, heads, d).permute(1, 0, 2)
+            v = rows[:, heads * d:].reshape(-1, heads, d).permute(1, 0, 2)
+            return k, v
+
+        o1, l1 = om.sdpa_lse(ql, *heads_of(kv_local))          # overlaps the gather
+        work.wait()
+        segs = qd.remote_segments(T, world, rank)
+        rem = torch.cat([kv_global[s:s + n] for s, n in segs])
+        o2, l2 = om.sdpa_lse(ql, *heads_of(rem))
+        o, lse = om.merge_attention([(o1, l1), (o2, l2)])
+        ref_o, ref_lse = om.sdpa_lse(ql, *heads_of(kv_global))
+        q.put((rank, float((o - ref_o).abs().max()), float((lse - ref_lse).abs().max()), segs))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_pass_global_attention_equals_full_world3():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world = 3
+    port = _free_port()
+    procs = [ctx.Process(target=_split_pass_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, eo, el, segs = q.get(timeout=300)
+        res[r] = (eo, el, segs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert res[r][0] <= 1e-5 and res[r][1] <= 1e-5, res[r]
+    assert res[0][2] == [(37, 74)] and res[1][2] == [(0, 37), (74, 37)] and res[2][2] == [(0, 74)]

@@ -1,11 +1,13 @@
-"""GPU, 2 ranks (NCCL): the frame-sharded aggregator equals the single-GPU one.
+"""GPU, 2 and 4 ranks (NCCL): the frame-sharded aggregator equals the single-GPU one.
 
-Runs as child processes, one per GPU, when at least 2 GPUs are visible
-(skipped otherwise).  Rank r owns frames [r*S/2, (r+1)*S/2); global blocks
-all-gather K/V over NCCL.  Rank 0 also runs the whole sequence alone on its
-GPU and compares: identical kernels and accumulation order per row, so the
-outputs agree to fp16 rounding (rel-L2 <= 1e-3).  NVLS is switched off
-(NCCL_NVLS_ENABLE=0) and no kernel reads peer memory.
+Runs as child processes, one per GPU, when enough GPUs are visible (skipped
+otherwise).  Rank r owns frames [r*S/N, (r+1)*S/N); global blocks all-gather
+K/V over NCCL while the rank attends to its own keys, then attend to the other
+ranks' keys and merge the two passes (at 4 ranks the middle ranks' remote keys
+are two segments).  Rank 0 also runs the whole sequence alone on its GPU and
+compares: rel-L2 <= 2e-3 (the split passes round each part to fp16 before the
+merge).  NVLS is switched off (NCCL_NVLS_ENABLE=0) and no kernel reads peer
+memory.
 """
 import os
 import socket
@@ -30,7 +32,7 @@ rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
 torch.cuda.set_device(rank)
 dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
 _lib.load()
-S = 4
+S = 8
 cfg = AggConfig(depth=2)
 f0, n = frame_shard(S, world, rank)
 m = random_vggt_aggregator(cfg, 7, torch.device("cuda", rank), n, dist.group.WORLD, world, rank, pe_depth=2)
@@ -46,7 +48,7 @@ if rank == 0:
     ref = single.forward(imgs.cuda())[-1][1].float().cpu()
     err = ((full - ref).norm() / ref.norm()).item()
     print("REL_L2", err, flush=True)
-    assert err <= 1e-3, err
+    assert err <= 2e-3, err
     assert _lib.device_status() == 0
 dist.barrier()
 dist.destroy_process_group()
@@ -61,13 +63,14 @@ def _port():
     return p
 
 
-def test_frame_sharded_aggregator_matches_single_gpu():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_frame_sharded_aggregator_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = _port()
     procs = []
-    for r in range(2):
-        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
                    MASTER_PORT=str(port), QV_ROOT=ROOT, NCCL_NVLS_ENABLE="0")
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
