@@ -292,6 +292,8 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--depth", type=int, default=24)
+    ap.add_argument("--no-overlap-kv", action="store_true",
+                    help="N > 1: attend only after the whole K/V all-gather (no local-keys pass during it)")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -315,6 +317,8 @@ def main():
     group = torch.distributed.group.WORLD if ws > 1 else None
     model = random_vggt_aggregator(cfg, seed=1234, device=dev, frames_local=S_local, group=group, world=ws,
                                    rank=rank, pe_depth=args.depth)
+    if args.no_overlap_kv:
+        model.runner.overlap_kv = False
     images = synthetic_images(S, seed=0)[rank * S_local:(rank + 1) * S_local].contiguous()
     img_dev = images.to(dev)
     img_host = images.pin_memory()

@@ -277,6 +277,17 @@ int qvggt_assemble_tokens(const void* src, int64_t src_rows_per_frame, int64_t s
                           int32_t n_special, int32_t two_sets, const void* pos, void* out, int64_t S, int32_t P,
                           int32_t C, int64_t frame_offset, void* stream);
 
+/* Kernel configuration of every large-M GEMM entry point (W4A16, dense fp16,
+ * int8): 0 = chosen per shape (default: the configuration with the fewest
+ * estimated cycles, waves of tiles over the SMs x time per tile), 1 = CTA
+ * pairs with 256 x 256 tiles, 2 = one SM per 128 x 256 tile, 3 = one SM per
+ * 128 x 128 tile.  A forced configuration a shape cannot use falls back to
+ * the automatic choice.  Process-wide; for tuning and tests.  The
+ * QVGGT_GEMM_CONFIG environment variable sets the initial value.  No
+ * reference counterpart (the reference picks its GEMM by M alone,
+ * gemm_cuda.cu:1154-1232). */
+int qvggt_set_gemm_config(int32_t cfg);
+
 /* ------------------------------------------------------------- self-test */
 
 /* Runs one kernel whose bounded wait waits on an mbarrier nothing arrives on;

@@ -10,6 +10,7 @@
     python profile_cases.py time                   # CUDA-event timings of all of the above
     python profile_cases.py sdpa                   # torch SDPA backends vs ours at the bench's attention shapes
     python profile_cases.py ranks [S]              # global attention of one rank of N = 1, 2, 4, 8 (split plans)
+    python profile_cases.py gemm_configs           # every GEMM kernel configuration at per-rank shapes
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
 launch) on seeded synthetic data sized above the 126 MB L2 where it matters.
@@ -261,6 +262,33 @@ def rank_shapes(S=32, iters=5):
         print("  ".join(row), flush=True)
 
 
+def gemm_configs(iters=10):
+    """The aggregator's linears at the per-rank row counts of 1, 2, 4 and 8
+    GPUs (S = 32) under each kernel configuration (1 = CTA pairs, 2 = 1-SM
+    256-wide, 3 = 1-SM 128-wide) and the automatic choice (0); W4A16 and
+    dense fp16 (the DINOv2 front), TFLOP/s."""
+    shapes = [(3072, 1024), (1024, 1024), (4096, 1024), (1024, 4096)]     # qkv, proj, fc1, fc2
+    for M in (43968, 21984, 10992, 5496):
+        for mode in ("w4", "f16"):
+            for N, K in shapes:
+                x = torch.randn(M, K, dtype=torch.float16, device="cuda")
+                out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+                if mode == "w4":
+                    qw, s, z = _w4(N, K)
+                    fn = lambda: eng.w4a16_linear(x, qw, s, z, out=out)
+                else:
+                    w = torch.randn(N, K, dtype=torch.float16, device="cuda") * 0.02
+                    fn = lambda: eng.f16_linear(x, w, out=out)
+                row = [f"{mode} M={M} N={N} K={K}:"]
+                for cfg in (0, 1, 2, 3):
+                    _lib.call("qvggt_set_gemm_config", cfg)
+                    fn()
+                    t = _time(fn, iters)
+                    row.append(f"cfg{cfg} {t * 1e6:.1f} us {2.0 * M * N * K / t / 1e12:.0f}")
+                _lib.call("qvggt_set_gemm_config", 0)
+                print("  ".join(row), flush=True)
+
+
 def _time(fn, iters=20, graph=False):
     """Average device time per call.  graph=True captures the `iters` calls in
     one CUDA graph first, so host launch overhead does not pace short kernels."""
@@ -309,6 +337,8 @@ def main(argv):
         forward_time(argv[1] if len(argv) > 1 else "w4", *(int(v) for v in argv[2:4]))
     elif what == "sdpa":
         sdpa_bar()
+    elif what == "gemm_configs":
+        gemm_configs()
     elif what == "ranks":
         rank_shapes(*(int(v) for v in argv[1:2]))
     elif what == "time":

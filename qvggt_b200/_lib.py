@@ -23,6 +23,7 @@ SIGNATURES = {
     "qvggt_last_error": [],
     "qvggt_device_status": [u32p, C.c_int],
     "qvggt_set_wait_timeout_ns": [u64],
+    "qvggt_set_gemm_config": [i32],
     "qvggt_launch_count": [],
     "qvggt_w4a16_gemm": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
     "qvggt_w4a16_linear_ex": [vp, i64, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, i64, vp, vp],

@@ -180,13 +180,21 @@ class AggregatorRunner:
         # With more than one rank the global attention runs as a local-keys
         # pass overlapping the K/V all-gather and a remote-keys pass
         # (overlap_kv), or after the whole gather (overlap_kv=False).
+        # Every global attention uses the library's split plan (split-KV when
+        # the local query blocks alone would leave a partial wave of CTAs).
+        # (A runner built on the CPU, e.g. to load or save a checkpoint, keeps
+        # one split: it never launches anything.)
         self.overlap_kv = overlap_kv and world > 1
-        if self.overlap_kv:
+        self.split_all = self.split_local = self.split_remote = 1
+        b0 = b1 = b2 = 0
+        if self.device.type == "cuda":
             with torch.cuda.device(self.device):
+                self.split_all, b0 = eng.attention_plan(1, self.T, self.T * world, cfg.heads)
                 self.split_local, b1 = eng.attention_plan(1, self.T, self.T, cfg.heads)
-                self.split_remote, b2 = eng.attention_plan(1, self.T, self.T * (world - 1), cfg.heads)
-            if max(b1, b2):
-                self.ws.attn_scratch = torch.empty(max(b1, b2), dtype=torch.uint8, device=self.device)
+                if world > 1:
+                    self.split_remote, b2 = eng.attention_plan(1, self.T, self.T * (world - 1), cfg.heads)
+        if max(b0, b1, b2):
+            self.ws.attn_scratch = torch.empty(max(b0, b1, b2), dtype=torch.uint8, device=self.device)
         # When a list: one dict per global-attention call, appended by the
         # global blocks: CUDA events ("passes": [(start, end), ...] around
         # each attention launch; "wait": (end of the local pass, gather landed)
@@ -244,7 +252,8 @@ class AggregatorRunner:
             e = [ev(), ev()] if timer is not None else None
             if e:
                 e[0].record()
-            eng.attention(ws.q, kv, cfg.heads, 1, T, Lkv, out=ws.attn)
+            eng.attention_ex(ws.q, kv, cfg.heads, 1, T, Lkv, out=ws.attn, splits=self.split_all,
+                             scratch=ws.attn_scratch)
             if e:
                 e[1].record()
                 timer.append({"passes": [(e[0], e[1])], "flop": 4.0 * T * Lkv * cfg.dim})

@@ -17,7 +17,10 @@
 // Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
 // warps 4..7 = epilogue (TMEM lane quarters 0..3), warps 8.. = dequantisation
 // (B_W4 only).  All inter-role waits are bounded (see common.cuh).
+#include <atomic>
+
 #include "gemm_common.cuh"
+
 #include "gemm_sm100.cuh"
 #include "host.hpp"
 
@@ -390,25 +393,83 @@ int gemm_launch(const GemmLaunch& L) {
   if (L.mode == B_I8 && L.epi != EPI_I32 && (!L.wscale || !L.ascale)) return set_error(QVGGT_ERR_INVALID, "gemm: w8a8 needs scales");
   if (L.M == 0) return QVGGT_OK;
 
-  const bool bn256 = (L.N % 256 == 0) && !L.force_bn128;
-  // CTA pairs (2-SM MMA, 256-row tiles) once there are enough rows to fill
-  // them.  Chosen per mode by measurement on B200 at the aggregator shapes
-  // (M = 43968, N = 4096, K = 1024): dense fp16 1213 vs 1078 TFLOP/s and
-  // W4A16 906 vs 825 on pairs; int8 1187 vs 1216 stays on the 1-SM kernel.
-  // QVGGT_GEMM_2SM=0 / =1 forces one kernel for every mode.
-  static int force_2sm = -2;
-  if (force_2sm == -2) {
-    const char* e = getenv("QVGGT_GEMM_2SM");
-    force_2sm = (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+  int cfg = gemm_config_override();
+  const bool can256 = (L.N % 256 == 0) && !L.force_bn128;
+  const bool can_pair = can256 && L.M >= 512;
+  if ((cfg == GEMM_CFG_PAIR && !can_pair) || (cfg == GEMM_CFG_1SM_256 && !can256)) cfg = GEMM_CFG_AUTO;
+  if (cfg == GEMM_CFG_AUTO) cfg = choose_gemm_config(L.mode, L.M, L.N, device_info().num_sms, can_pair, can256);
+  switch (cfg) {
+    case GEMM_CFG_PAIR: return gemm_launch_2sm(L);
+    case GEMM_CFG_1SM_256:
+      switch (L.mode) {
+        case B_W4: return launch_gemm<256, B_W4>(L);
+        case B_F16: return launch_gemm<256, B_F16>(L);
+        default: return launch_gemm<256, B_I8>(L);
+      }
+    default:
+      switch (L.mode) {
+        case B_W4: return launch_gemm<128, B_W4>(L);
+        case B_F16: return launch_gemm<128, B_F16>(L);
+        default: return launch_gemm<128, B_I8>(L);
+      }
   }
-  const bool pair_mode = force_2sm >= 0 ? force_2sm == 1 : (L.mode == B_F16 || L.mode == B_W4);
-  if (pair_mode && bn256 && L.M >= 512) return gemm_launch_2sm(L);
-  switch (L.mode) {
-    case B_W4: return bn256 ? launch_gemm<256, B_W4>(L) : launch_gemm<128, B_W4>(L);
-    case B_F16: return bn256 ? launch_gemm<256, B_F16>(L) : launch_gemm<128, B_F16>(L);
-    case B_I8: return bn256 ? launch_gemm<256, B_I8>(L) : launch_gemm<128, B_I8>(L);
+}
+
+// Tuning override of the kernel configuration (-1: not read from the
+// environment yet).  Set by qvggt_set_gemm_config.
+std::atomic<int> g_gemm_cfg{-1};
+
+int gemm_config_override() {
+  int c = g_gemm_cfg.load(std::memory_order_relaxed);
+  if (c < 0) {
+    // QVGGT_GEMM_CONFIG = 0 (auto), 1 (CTA pairs), 2 (1-SM, 256-wide), 3 (1-SM, 128-wide)
+    const char* e = getenv("QVGGT_GEMM_CONFIG");
+    c = (e && e[0] >= '0' && e[0] <= '3' && e[1] == 0) ? e[0] - '0' : GEMM_CFG_AUTO;
+    g_gemm_cfg.store(c, std::memory_order_relaxed);
   }
-  return set_error(QVGGT_ERR_INVALID, "gemm: bad mode");
+  return c;
+}
+
+// Kernel configuration for an M x N GEMM: the one with the least estimated
+// time = (waves of tiles over the SMs) x (time of one tile).  Throughput of
+// each kernel per SM, measured on B200 with the SMs full (M = 43,968,
+// K = 1024): dense fp16 pairs 1213, 1-SM 256-wide 1078, 128-wide ~960 TFLOP/s;
+// W4A16 pairs ~1000, 1-SM 830 / ~740; int8 (no pair form) 1216 / ~1080 TOPS.
+// A pair tile is 256 x 256 on two SMs, a 1-SM tile 128 x BN on one.  At the
+// aggregator's full shapes this keeps pairs for fp16 / W4 and the 1-SM
+// 256-wide kernel for int8; a rank of a frame-sharded run (M = 5,496 at 8
+// GPUs) switches the N = 1024 GEMMs, which as pair tiles fill 1.2 waves, to
+// 128-wide 1-SM tiles.
+int choose_gemm_config(int mode, long long M, long long N, int sms, bool can_pair, bool can256) {
+  static const double rate[3][3] = {// [mode][pair, 1sm256, 1sm128]
+                                    {1000.0, 830.0, 740.0},
+                                    {1213.0, 1078.0, 960.0},
+                                    {0.0, 1216.0, 1080.0}};
+  const int m = mode < 0 || mode > 2 ? 1 : mode;
+  double best = 1e300;
+  int pick = GEMM_CFG_1SM_128;
+  auto consider = [&](int cfg, long long tiles, int slots, double tile_flop, double r) {
+    if (r <= 0.0 || slots <= 0) return;
+    const double waves = (double)((tiles + slots - 1) / slots);
+    const double t = waves * tile_flop / r;   // per-SM work of one tile over that SM's share of the rate
+    if (t < best * 0.98) {
+      best = t;
+      pick = cfg;
+    }
+  };
+  const long long m128 = (M + 127) / 128, m256 = (M + 255) / 256;
+  consider(GEMM_CFG_1SM_128, m128 * (N / 128), sms, 128.0 * 128.0, rate[m][2]);
+  if (can256) consider(GEMM_CFG_1SM_256, m128 * (N / 256), sms, 128.0 * 256.0, rate[m][1]);
+  if (can_pair) consider(GEMM_CFG_PAIR, m256 * (N / 256), sms / 2, 128.0 * 256.0, rate[m][0]);
+  return pick;
 }
 
 }  // namespace qv
+
+extern "C" int qvggt_set_gemm_config(int32_t cfg) {
+  if (cfg < qv::GEMM_CFG_AUTO || cfg > qv::GEMM_CFG_1SM_128)
+    return qv::set_error(QVGGT_ERR_INVALID, "set_gemm_config: %d is not 0 (auto), 1 (pairs), 2 or 3 (1-SM)", cfg);
+  qv::g_gemm_cfg.store(cfg, std::memory_order_relaxed);
+  return QVGGT_OK;
+}
+

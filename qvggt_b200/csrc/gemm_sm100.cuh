@@ -53,6 +53,11 @@ struct GemmLaunch {
 };
 
 int gemm_launch(const GemmLaunch& L);
+
+// Kernel configurations of gemm_launch (its choice, or a tuning override).
+enum GemmConfig { GEMM_CFG_AUTO = 0, GEMM_CFG_PAIR = 1, GEMM_CFG_1SM_256 = 2, GEMM_CFG_1SM_128 = 3 };
+int gemm_config_override();   // GEMM_CFG_AUTO unless qvggt_set_gemm_config / QVGGT_GEMM_CONFIG say otherwise
+int choose_gemm_config(int mode, long long M, long long N, int sms, bool can_pair, bool can256);
 // 2-SM (CTA-pair) variant for large M; called by gemm_launch after validation.
 int gemm_launch_2sm(const GemmLaunch& L);
 

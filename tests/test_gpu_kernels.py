@@ -347,41 +347,53 @@ def test_qkv_rope_linear_matches_separate_path(kind, qk_norm):
 
 
 @pytest.mark.parametrize("mode", ["w4", "f16", "i8"])
-def test_pair_gemm_equals_single_sm_gemm(mode):
-    """With QVGGT_GEMM_2SM=1, M >= 512 runs on CTA pairs (2-SM MMA, 256-row
-    tiles) and M < 512 on the 1-SM kernel: the rows both compute must agree bit
-    for bit (same K order).  Runs in a child process (the switch is read once)."""
-    import os
-    import subprocess
-    import sys
-    if os.environ.get("QVGGT_GEMM_2SM") != "1":
-        env = dict(os.environ, QVGGT_GEMM_2SM="1")
-        r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", "-m", "gpu",
-                            f"{__file__}::test_pair_gemm_equals_single_sm_gemm[{mode}]"],
-                           env=env, capture_output=True, text=True, timeout=300)
-        assert r.returncode == 0, r.stdout[-3000:]
-        return
+def test_gemm_configs_agree_bit_for_bit(mode):
+    """Every kernel configuration of the large-M GEMM (CTA pairs with 256-row
+    tiles, 1-SM 128 x 256 and 128 x 128 tiles; ``qvggt_set_gemm_config``)
+    accumulates each output over K in the same order, so all of them agree bit
+    for bit, and with the oracle within the per-linear bound.  int8 has no pair
+    form (that setting falls back to the automatic choice)."""
+    from qvggt_b200 import _lib
     from qvggt_b200 import awq_inference_engine as eng
     M, N, K = 1024, 512, 1024
     g = torch.Generator().manual_seed(31)
     if mode == "i8":
         a = torch.randint(-128, 128, (M, K), dtype=torch.int8, generator=g).to(DEV)
         w = torch.randint(-128, 128, (N, K), dtype=torch.int8, generator=g).to(DEV)
-        full, part = eng.i8_gemm_i32(a, w), eng.i8_gemm_i32(a[:384].contiguous(), w)
-        assert np.array_equal(full.cpu().numpy(), ow.int8_gemm_i32(a.cpu().numpy(), w.cpu().numpy()))
+        f = lambda: eng.i8_gemm_i32(a, w)
+        ref = None
     else:
         x = torch.randn(M, K, generator=g).half().to(DEV)
         if mode == "w4":
             lin, t = _lin(N, K, 128, seed=3)
-            f = lambda xx: eng.gemm_forward_cuda_new(xx, t["qweight"], t["scales"], t["scaled_zeros"])
+            f = lambda: eng.gemm_forward_cuda_new(x, t["qweight"], t["scales"], t["scaled_zeros"])
             ref = awq.w4a16_linear(x.cpu(), lin["qweight"], lin["scales"], lin["scaled_zeros"], 128)
         else:
             wt = (torch.randn(N, K, generator=g) * 0.02).half()
-            f = lambda xx: eng.f16_linear(xx, wt.to(DEV))
+            f = lambda: eng.f16_linear(x, wt.to(DEV))
             ref = om.QLinear("f16", weight=wt, bias=None)(x.cpu()).float()
-        full, part = f(x), f(x[:384].contiguous())
-        assert awq.max_abs_rel(full.cpu(), ref) <= 2e-3
-    assert torch.equal(full[:384], part)
+    outs = []
+    try:
+        for cfg in (1, 2, 3):
+            _lib.call("qvggt_set_gemm_config", cfg)
+            outs.append(f().clone())
+    finally:
+        _lib.call("qvggt_set_gemm_config", 0)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    if mode == "i8":
+        assert np.array_equal(outs[0].cpu().numpy(), ow.int8_gemm_i32(a.cpu().numpy(), w.cpu().numpy()))
+    else:
+        assert awq.max_abs_rel(outs[0].cpu(), ref) <= 2e-3
+
+
+def test_gemm_config_choice():
+    """The automatic choice keeps CTA pairs at the aggregator's full shapes and
+    rejects an unknown setting."""
+    from qvggt_b200 import _lib
+    from qvggt_b200._lib import QvggtError
+    with pytest.raises(QvggtError):
+        _lib.call("qvggt_set_gemm_config", 7)
 
 
 @pytest.mark.parametrize("M,N", [(4096, 4096), (10992, 3072)])
