@@ -432,19 +432,19 @@ int gemm_config_override() {
 
 // Kernel configuration for an M x N GEMM: the one with the least estimated
 // time = (waves of tiles over the SMs) x (time of one tile).  Throughput of
-// each kernel per SM, measured on B200 with the SMs full (M = 43,968,
-// K = 1024): dense fp16 pairs 1213, 1-SM 256-wide 1078, 128-wide ~960 TFLOP/s;
-// W4A16 pairs ~1000, 1-SM 830 / ~740; int8 (no pair form) 1216 / ~1080 TOPS.
-// A pair tile is 256 x 256 on two SMs, a 1-SM tile 128 x BN on one.  At the
-// aggregator's full shapes this keeps pairs for fp16 / W4 and the 1-SM
-// 256-wide kernel for int8; a rank of a frame-sharded run (M = 5,496 at 8
-// GPUs) switches the N = 1024 GEMMs, which as pair tiles fill 1.2 waves, to
-// 128-wide 1-SM tiles.
+// each kernel with the SMs full, measured on B200 at M = 43,968 over the
+// aggregator's four linears (`profile_cases.py gemm_configs`): dense fp16
+// pairs 1110-1320, 1-SM 256-wide 1000-1190, 128-wide 730-850 TFLOP/s; W4A16
+// pairs 910-1090, 1-SM 700-780 / 530-560; int8 (no pair form) 1216 TOPS on
+// the 256-wide kernel.  A pair tile is 256 x 256 on two SMs, a 1-SM tile
+// 128 x BN on one.  With these rates pairs win for fp16 and W4A16 at every
+// row count of the frame-sharded runs (5,496 to 43,968 rows; measured the
+// same way), int8 takes the 256-wide 1-SM kernel.
 int choose_gemm_config(int mode, long long M, long long N, int sms, bool can_pair, bool can256) {
   static const double rate[3][3] = {// [mode][pair, 1sm256, 1sm128]
-                                    {1000.0, 830.0, 740.0},
-                                    {1213.0, 1078.0, 960.0},
-                                    {0.0, 1216.0, 1080.0}};
+                                    {1000.0, 760.0, 540.0},
+                                    {1250.0, 1100.0, 780.0},
+                                    {0.0, 1216.0, 850.0}};
   const int m = mode < 0 || mode > 2 ? 1 : mode;
   double best = 1e300;
   int pick = GEMM_CFG_1SM_128;
