@@ -11,6 +11,7 @@
     python profile_cases.py sdpa                   # torch SDPA backends vs ours at the bench's attention shapes
     python profile_cases.py ranks [S]              # global attention of one rank of N = 1, 2, 4, 8 (split plans)
     python profile_cases.py gemm_configs           # every GEMM kernel configuration at per-rank shapes
+    python profile_cases.py gemv [N] [K] [m]       # the W4A16 GEMV alone (two launches, one weight set)
 
 Each case launches its kernel twice (so `ncu -s 1 -c 1` captures a warm
 launch) on seeded synthetic data sized above the 126 MB L2 where it matters.
@@ -86,6 +87,19 @@ def mem(reps=2):
         for _ in range(reps):
             f()
     return fns
+
+
+def gemv(N=4096, K=4096, m=1, reps=2):
+    """The GEMV on one weight set, launched `reps` times (ncu -s 1 -c 1
+    captures a warm-launch of the same kernel; ncu flushes the caches before
+    each replay, so its DRAM figures are those of a cold read of the weights)."""
+    qw, s, z = _w4(N, K)
+    x = torch.randn(m, K, dtype=torch.float16, device="cuda")
+    fn = lambda: eng.gemv_forward_cuda_new(x, qw, s, z, m, N, K, 128)
+    for _ in range(reps):
+        fn()
+    nbytes = N * K // 2 + 2 * (K // 128) * N * 2 + m * K * 2 + m * N * 2
+    return fn, nbytes
 
 
 def small(M=32, N=6144, K=2048, reps=2):
@@ -327,6 +341,8 @@ def main(argv):
         gemm(argv[1] if len(argv) > 1 else "f16", *(int(v) for v in argv[2:3]))
     elif what == "mem":
         mem()
+    elif what == "gemv":
+        gemv(*(int(v) for v in argv[1:4]))
     elif what == "small":
         small(*(int(v) for v in argv[1:4]))
     elif what == "small_time":
