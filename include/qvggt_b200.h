@@ -246,6 +246,23 @@ int qvggt_attention_plan(int64_t batches, int64_t Lq, int64_t keys, int32_t head
 int qvggt_attention_scratch_bytes(int64_t batches, int64_t Lq, int32_t heads, int32_t splits,
                                   int64_t* scratch_bytes);
 
+/* qvggt_attention_ex over all keys (lse_mode 0) with `splits` (1..4) split-KV
+ * CTAs, for callers that cannot allocate device memory: it allocates nothing.
+ * Its scratch is a fixed 64 MiB array in the library's device memory, present
+ * on every GPU that loads the library until the process exits; a shape whose
+ * scratch (qvggt_attention_scratch_bytes) exceeds 64 MiB is rejected with
+ * QVGGT_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that
+ * first call before any stream capture.  All calls on a device share the array
+ * and leave their data in it; each call clears the counters it needs on
+ * `stream` before its kernel, so calls in order on one stream are safe, and
+ * calls whose kernels may run at the same time on the GPU (other streams,
+ * other host threads) race.  Same arguments and results as qvggt_attention_ex.
+ * No counterpart in the reference. */
+int qvggt_attention_split_static(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride,
+                                 int64_t k_col0, int64_t v_col0, void* out, int64_t o_stride, int64_t batches,
+                                 int64_t Lq, int64_t Lkv, int32_t heads, int32_t splits, void* stream);
+
 /* Attention over short sequences with head_dim 128 (the camera-head trunk:
  * 16 heads x 128 over the S <= 256 camera tokens of each batch),
  * softmax(q k^T / sqrt(128)) v on CUDA cores in fp32.  Same token-major

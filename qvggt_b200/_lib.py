@@ -47,6 +47,7 @@ SIGNATURES = {
                            vp, i64, vp],
     "qvggt_attention_plan": [i64, i64, i64, i32, C.POINTER(i32), i64p],
     "qvggt_attention_scratch_bytes": [i64, i64, i32, i32, i64p],
+    "qvggt_attention_split_static": [vp, i64, vp, i64, i64, i64, vp, i64, i64, i64, i64, i32, i32, vp],
     "qvggt_attention_small": [vp, i64, vp, i64, i64, i64, vp, i64, i64, i64, i32, vp],
     "qvggt_selftest_wait_timeout": [u64, u32p],
     "qvggt_patchify": [vp, vp, i64, i32, i32, i32, i32, C.POINTER(f32), C.POINTER(f32), vp],

@@ -40,6 +40,7 @@
 // (common.cuh).
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #include "host.hpp"
 
@@ -926,4 +927,60 @@ extern "C" int qvggt_attention_scratch_bytes(int64_t batches, int64_t Lq, int32_
     return set_error(QVGGT_ERR_INVALID, "attention_scratch_bytes: bad arguments");
   *scratch_bytes = scratch_layout(batches, Lq, heads, splits).total;
   return QVGGT_OK;
+}
+
+// ------------------------------------------------------------------------
+// Split-KV attention whose scratch lives in a fixed device array, for callers
+// that may not allocate device memory: an allocator-less host runtime, code
+// that runs while memory is being handed out by someone else (inside a memory
+// pool's callback, a custom allocator, or a region where the owner forbids new
+// allocations), or an integration that owns every byte of the GPU and cannot
+// let a library call cudaMalloc behind its back.
+namespace qv {
+namespace {
+
+// 64 MiB on every device that loads this library, held until the process
+// exits.  It holds the split counters, the per-split log-sum-exps and the
+// per-split fp32 output rows: splits * batches * heads * Lq rows of 260 bytes
+// plus alignment (e.g. 2 splits of 16 heads x 5,496 queries, one rank of the
+// 8-GPU aggregator, take 45.7 MB).
+constexpr long long STATIC_SCRATCH_BYTES = 64LL << 20;
+static __device__ __align__(256) uint8_t g_attn_static_scratch[STATIC_SCRATCH_BYTES];
+
+// The array's device address, looked up once per device with that device
+// current.  (In host code the array's name is a host-side stand-in, not an
+// address a kernel may be given.)
+std::once_flag g_static_once[kMaxDevices];
+void* g_static_ptr[kMaxDevices] = {};
+cudaError_t g_static_err[kMaxDevices] = {};
+
+}  // namespace
+}  // namespace qv
+
+extern "C" int qvggt_attention_split_static(const void* q, int64_t q_stride, const void* kv, int64_t kv_stride,
+                                            int64_t k_col0, int64_t v_col0, void* out, int64_t o_stride,
+                                            int64_t batches, int64_t Lq, int64_t Lkv, int32_t heads, int32_t splits,
+                                            void* stream) {
+  int dev = -1;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "attention_split_static: cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "attention_split_static: device %d beyond the %d this library tracks", dev,
+                     kMaxDevices);
+  if (splits < 1 || splits > MAX_SPLITS)
+    return set_error(QVGGT_ERR_INVALID, "attention_split_static: splits must be in 1..%d", MAX_SPLITS);
+  if (batches < 0 || Lq < 0 || heads <= 0) return set_error(QVGGT_ERR_INVALID, "attention_split_static: bad shape");
+  const long long need = scratch_layout(batches, Lq, heads, splits).total;
+  if (need > STATIC_SCRATCH_BYTES)
+    return set_error(QVGGT_ERR_UNSUPPORTED,
+                     "attention_split_static: %d splits of %lld batches x %d heads x %lld queries need %lld bytes of "
+                     "scratch; the fixed array holds %lld (use fewer splits or qvggt_attention_ex with your own scratch)",
+                     splits, (long long)batches, heads, (long long)Lq, need, STATIC_SCRATCH_BYTES);
+  std::call_once(g_static_once[dev], [dev] {
+    g_static_err[dev] = cudaGetSymbolAddress(&g_static_ptr[dev], g_attn_static_scratch);
+  });
+  if (g_static_err[dev] != cudaSuccess || g_static_ptr[dev] == nullptr)
+    return set_error(QVGGT_ERR_CUDA, "attention_split_static: cudaGetSymbolAddress: %s",
+                     cudaGetErrorString(g_static_err[dev]));
+  return attention_launch(q, q_stride, kv, kv_stride, k_col0, v_col0, out, o_stride, batches, Lq, Lkv, 0, Lkv, 0, 0,
+                          heads, splits, 0, nullptr, g_static_ptr[dev], STATIC_SCRATCH_BYTES, stream);
 }
