@@ -1,94 +1,121 @@
 // W4A16 GEMV for 1 <= m <= 16 rows: out[m, N] = x[m, K] . deq(W)^T (+ bias).
 //
-// HBM-bound on the packed weights (N*K/2 bytes).  One CTA of 4 warps per
-// packed row g (output channels 4g..4g+3); each lane streams 16-byte chunks of
-// the packed row with 128-bit loads (a 16-byte chunk = 32 nibbles of one
-// channel over 32 consecutive k), dequantises them bit-exactly (same
-// arithmetic as the GEMM and the reference's __hfma2), and accumulates
-// x . w in fp32.  Partial sums are reduced with warp shuffles, then across the
-// 4 warps through shared memory.
+// HBM-bound on the packed weights (N*K/2 bytes), and at the sizes it runs on
+// (a few MB) bound just as much by how fast all of them are in flight and how
+// well the dequantisation's dependent ALU chains are interleaved.  Four warps
+// per packed row g (output channels 4g..4g+3), four rows per 512-thread CTA
+// (N = 4096 is 256 CTAs, two resident per SM, all in flight at once): each
+// lane issues 4 128-bit loads of its quarter of the row (a 16-byte chunk = 32
+// nibbles of one channel over 32 consecutive k) plus their scales and zeros
+// before using any, x is staged once per CTA in shared memory by asynchronous
+// copies issued first, and each channel's sum is reduced with three shuffles
+// within a warp and then over the row's four warps in shared memory.
+// Weights are dequantised bit-exactly (same arithmetic as the GEMM and the
+// reference's __hfma2); x . w is formed over each run of 8 consecutive k with
+// fp16x2 FMAs and that partial is added into an fp32 accumulator (the
+// reference's GEMV accumulates every product of a thread in fp16; a product
+// is exact when x is one-hot).
 #include "host.hpp"
 
 namespace qv {
 namespace {
 
-template <int MT, int MAXIT>
-__global__ void __launch_bounds__(128) gemv_w4_kernel(const __half* __restrict__ x, const uint16_t* __restrict__ qw,
-                                                      const __half* __restrict__ scales,
-                                                      const __half* __restrict__ zeros, const __half* __restrict__ bias,
-                                                      __half* __restrict__ out, int m, int N, int K, int G) {
-  __shared__ float red[4][4][MT];
-  const int g = blockIdx.x;           // packed row
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint8_t* row = reinterpret_cast<const uint8_t*>(qw + (size_t)g * K);
-  const int row_bytes = K * 2;
-  float acc[MT];
-#pragma unroll
-  for (int i = 0; i < MT; ++i) acc[i] = 0.f;
+constexpr int GEMV_ROWS = 4;              // packed rows per CTA
+constexpr int GEMV_WARPS = 4 * GEMV_ROWS; // four warps per packed row
+constexpr int GEMV_BATCH = 4;             // 16-byte chunks per lane in flight
+constexpr int GEMV_XS_MAX = 32768;        // x staged in shared memory up to this many bytes
 
-  // Byte offset of this lane's chunk: ((it*4 + warp)*32 + lane)*16.  Within a
-  // 128-byte k-chunk c: channel i = (off%128)/32, half h = (off%32)/16.
-  const int ci = (lane & 7) >> 1;   // constant over iterations (stride is a multiple of 128 B)
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+
+template <int MT, bool XS>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kernel(
+    const __half* __restrict__ x, const uint16_t* __restrict__ qw, const __half* __restrict__ scales,
+    const __half* __restrict__ zeros, const __half* __restrict__ bias, __half* __restrict__ out, int m, int N, int K,
+    int G) {
+  extern __shared__ __align__(16) __half x_smem[];   // XS: x [m, K]
+  __shared__ float red[GEMV_ROWS][4][4][MT];          // [row][quarter][channel][m]
+  if constexpr (XS) {
+    const int chunks = m * K / 8;
+    for (int q = threadIdx.x; q < chunks; q += blockDim.x) cp_async16(smem_u32(x_smem + 8 * q), x + 8 * q);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rw = warp >> 2, wq = warp & 3;            // row of the CTA, quarter of the row
+  const int g = blockIdx.x * GEMV_ROWS + rw;          // packed row of this warp
+  const bool active = g < N / 4;
+  const uint8_t* row = reinterpret_cast<const uint8_t*>(qw + (size_t)(active ? g : 0) * K);
+  const int row_bytes = K * 2;
+  // Chunk it of a batch sits at byte base + ((it*4 + wq)*32 + lane)*16; within
+  // a 128-byte k-chunk c that is channel ci = (lane%8)/2, half h = lane%2.
+  const int ci = (lane & 7) >> 1;
   const int h = lane & 1;
   const __half2 magic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  // Issue every weight (and scale / zero) load of this thread before any math,
-  // so up to MAXIT 16-byte loads per thread are in flight at once.
-  uint4 wvs[MAXIT];
-  __half ss[MAXIT], zs[MAXIT];
-  const int off0 = (warp * 32 + lane) * 16;
+  float acc[MT];
 #pragma unroll
-  for (int it = 0; it < MAXIT; ++it) {
-    const int off = off0 + it * 128 * 16;
-    if (off < row_bytes) {
-      wvs[it] = __ldg(reinterpret_cast<const uint4*>(row + off));
-      const int grp = (64 * (off >> 7) + 32 * h) / G;
-      ss[it] = scales[(size_t)grp * N + 4 * g + ci];
-      zs[it] = zeros[(size_t)grp * N + 4 * g + ci];
-    }
-  }
+  for (int r = 0; r < MT; ++r) acc[r] = 0.f;
+  for (int base = 0; base < row_bytes; base += GEMV_BATCH * 2048) {
+    uint4 wvs[GEMV_BATCH];
+    __half ss[GEMV_BATCH], zs[GEMV_BATCH];
 #pragma unroll
-  for (int it = 0; it < MAXIT; ++it) {
-    const int off = off0 + it * 128 * 16;
-    if (off >= row_bytes) break;
-    const int c = off >> 7;
-    const int k0 = 64 * c + 32 * h;
-    const uint4 wv = wvs[it];
-    const __half2 s2 = __half2half2(ss[it]), z2 = __half2half2(zs[it]);
-    const uint32_t xs[4] = {wv.x, wv.y, wv.z, wv.w};
-    // w[q][u] covers k = k0 + 8q + 2u, +1
-    float2 w[4][4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        uint32_t t;
-        const uint32_t src = xs[u] >> (4 * q);
-        asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(0x64006400u));
-        __half2 hq = __hsub2(*reinterpret_cast<__half2*>(&t), magic);
-        w[q][u] = __half22float2(__hfma2(hq, s2, z2));
+    for (int it = 0; it < GEMV_BATCH; ++it) {
+      const int off = base + ((it * 4 + wq) * 32 + lane) * 16;
+      if (active && off < row_bytes) {
+        wvs[it] = __ldg(reinterpret_cast<const uint4*>(row + off));
+        const int grp = (64 * (off >> 7) + 32 * h) / G;
+        ss[it] = scales[(size_t)grp * N + 4 * g + ci];
+        zs[it] = zeros[(size_t)grp * N + 4 * g + ci];
       }
     }
+    if (XS && base == 0) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+    }
+    if (!active) continue;
 #pragma unroll
-    for (int r = 0; r < MT; ++r) {
-      if (r < m) {
-        const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)r * K + k0);
-        float a = acc[r];
+    for (int it = 0; it < GEMV_BATCH; ++it) {
+      const int off = base + ((it * 4 + wq) * 32 + lane) * 16;
+      if (off >= row_bytes) break;
+      const int k0 = 64 * (off >> 7) + 32 * h;
+      const uint4 wv = wvs[it];
+      const __half2 s2 = __half2half2(ss[it]), z2 = __half2half2(zs[it]);
+      const uint32_t xw[4] = {wv.x, wv.y, wv.z, wv.w};
+      // w[q][u] (dequantised fp16 pair) covers k = k0 + 8q + 2u, +1
+      __half2 w[4][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 xv = __ldg(xp + q);
-          const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+      for (int q = 0; q < 4; ++q) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float2 xf = unpack_half2(xu[u]);
-            a = fmaf(xf.x, w[q][u].x, a);
-            a = fmaf(xf.y, w[q][u].y, a);
-          }
+        for (int u = 0; u < 4; ++u) {
+          uint32_t t;
+          const uint32_t src = xw[u] >> (4 * q);
+          asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(0x64006400u));
+          __half2 hq = __hsub2(*reinterpret_cast<__half2*>(&t), magic);
+          w[q][u] = __hfma2(hq, s2, z2);
         }
-        acc[r] = a;
+      }
+#pragma unroll
+      for (int r = 0; r < MT; ++r) {
+        if (r < m) {
+          const uint4* xp = reinterpret_cast<const uint4*>((XS ? x_smem : x) + (size_t)r * K + k0);
+          float a = acc[r];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 xv = XS ? xp[q] : __ldg(xp + q);
+            const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+            // x . w over these 8 k in fp16x2, then one fp32 add per half
+            __half2 p = __hmul2(*reinterpret_cast<const __half2*>(&xu[0]), w[q][0]);
+#pragma unroll
+            for (int u = 1; u < 4; ++u) p = __hfma2(*reinterpret_cast<const __half2*>(&xu[u]), w[q][u], p);
+            const float2 pf = __half22float2(p);
+            a += pf.x + pf.y;
+          }
+          acc[r] = a;
+        }
       }
     }
   }
-  // Lanes sharing channel ci: lane%8 in {2ci, 2ci+1}, lane/8 in 0..3.
+  // lanes holding channel ci: lane%8 in {2ci, 2ci+1}, lane/8 in 0..3
 #pragma unroll
   for (int r = 0; r < MT; ++r) {
     float v = acc[r];
@@ -99,18 +126,19 @@ __global__ void __launch_bounds__(128) gemv_w4_kernel(const __half* __restrict__
   }
   if (lane < 8 && (lane & 1) == 0) {
 #pragma unroll
-    for (int r = 0; r < MT; ++r) red[warp][ci][r] = acc[r];
+    for (int r = 0; r < MT; ++r) red[rw][wq][ci][r] = acc[r];
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < 4 * m; idx += blockDim.x) {
-    const int r = idx >> 2, ch = idx & 3;
-    float v = red[0][ch][r] + red[1][ch][r] + red[2][ch][r] + red[3][ch][r];
-    const int n = 4 * g + ch;
-    if (r < MT) {
-      float y = round_f16(v);
-      if (bias) y = y + __half2float(bias[n]);
-      out[(size_t)r * N + n] = __float2half_rn(y);
-    }
+  // the row's four quarters, summed in a fixed order
+  for (int idx = threadIdx.x; idx < GEMV_ROWS * 4 * m; idx += blockDim.x) {
+    const int r = idx % m, ch = (idx / m) % 4, rr = idx / (4 * m);
+    const int gg = blockIdx.x * GEMV_ROWS + rr;
+    if (gg >= N / 4 || r >= MT) continue;
+    const float v = red[rr][0][ch][r] + red[rr][1][ch][r] + red[rr][2][ch][r] + red[rr][3][ch][r];
+    const int n = 4 * gg + ch;
+    float y = round_f16(v);
+    if (bias) y = y + __half2float(bias[n]);
+    out[(size_t)r * N + n] = __float2half_rn(y);
   }
 }
 
@@ -132,22 +160,22 @@ extern "C" int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const
   if (!aligned16(in_feats) || !aligned16(qweight))
     return set_error(QVGGT_ERR_ALIGN, "gemv: in_feats / qweight must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 grid((unsigned)(N / 4)), block(128);
+  const dim3 grid((unsigned)((N / 4 + GEMV_ROWS - 1) / GEMV_ROWS)), block(GEMV_WARPS * 32);
+  // x staged in shared memory when it fits the default 48 KB with room to spare
+  const int xs_bytes = (int)(m * K * 2);
+  const bool xs = xs_bytes <= GEMV_XS_MAX;
   auto args = [&](auto kfn) {
-    kfn<<<grid, block, 0, st>>>(static_cast<const __half*>(in_feats), static_cast<const uint16_t*>(qweight),
-                                static_cast<const __half*>(scales), static_cast<const __half*>(scaled_zeros),
-                                static_cast<const __half*>(bias), static_cast<__half*>(out), (int)m, (int)N, (int)K,
-                                group_size);
+    kfn<<<grid, block, xs ? xs_bytes : 0, st>>>(static_cast<const __half*>(in_feats),
+                                                 static_cast<const uint16_t*>(qweight),
+                                                 static_cast<const __half*>(scales),
+                                                 static_cast<const __half*>(scaled_zeros),
+                                                 static_cast<const __half*>(bias), static_cast<__half*>(out), (int)m,
+                                                 (int)N, (int)K, group_size);
   };
-  // 16-byte chunks per thread: a packed row is 2K bytes, a CTA covers 2 KB per pass
-  const int iters = (int)((K * 2 + 2047) / 2048);
   auto by_m = [&](auto mt) {
     constexpr int MT = decltype(mt)::value;
-    if (iters <= 1) args(gemv_w4_kernel<MT, 1>);
-    else if (iters <= 2) args(gemv_w4_kernel<MT, 2>);
-    else if (iters <= 4) args(gemv_w4_kernel<MT, 4>);
-    else if (iters <= 8) args(gemv_w4_kernel<MT, 8>);
-    else args(gemv_w4_kernel<MT, 16>);
+    if (xs) args(gemv_w4_kernel<MT, true>);
+    else args(gemv_w4_kernel<MT, false>);
   };
   if (K > 16384) return set_error(QVGGT_ERR_UNSUPPORTED, "gemv: K=%lld > 16384", (long long)K);
   if (m <= 1) by_m(std::integral_constant<int, 1>());
