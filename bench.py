@@ -274,7 +274,7 @@ def check_against_one_gpu(model, cfg, args, ws, rank, dev, img_dev, S, S_local):
     if rank == 0:
         full = torch.cat(parts).float()
         one = random_vggt_aggregator(cfg, seed=1234, device=dev, frames_local=S, pe_depth=args.depth)
-        ref = one.forward(synthetic_images(S, seed=0).to(dev))[-1][1].float()
+        ref = one.forward(synthetic_images(S, seed=args.seed).to(dev))[-1][1].float()
         res = {"rel_l2_vs_1gpu": float((full - ref).norm() / ref.norm()), "frames": S,
                "what": "last pair's global-block output, all ranks gathered, vs a one-GPU forward on the same seeds"}
         del one
@@ -289,6 +289,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--frames", type=int, default=32)
+    ap.add_argument("--seed", type=int, default=0, help="image seed (BASELINE config 2: 0, config 4: 1)")
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--depth", type=int, default=24)
@@ -319,7 +320,7 @@ def main():
                                    rank=rank, pe_depth=args.depth)
     if args.no_overlap_kv:
         model.runner.overlap_kv = False
-    images = synthetic_images(S, seed=0)[rank * S_local:(rank + 1) * S_local].contiguous()
+    images = synthetic_images(S, seed=args.seed)[rank * S_local:(rank + 1) * S_local].contiguous()
     img_dev = images.to(dev)
     img_host = images.pin_memory()
     out_host = torch.empty(S_local, cfg.tokens_per_frame, 2 * cfg.dim, dtype=torch.float16, pin_memory=True)
@@ -389,7 +390,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * t_dev / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (seeded U[0,1] 518x518 frames, random-init VGGT-1B weights quantised W4A16 g128)",
+            "data": f"synthetic (U[0,1] 518x518 frames, seed {args.seed}; random-init VGGT-1B weights quantised "
+                    f"W4A16 g128)",
             "config": {"workload": f"VGGT-1B aggregator forward (DINOv2 ViT-L/14 fp16 front + {args.depth} W4A16 "
                                    f"frame/global pairs), S={S} frames, 518x518",
                        "frames": S, "frames_per_gpu": S_local, "tokens_per_frame": cfg.tokens_per_frame,
