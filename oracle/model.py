@@ -293,13 +293,54 @@ def aggregator_tokens(pe_out: torch.Tensor, specials: torch.Tensor, frame_offset
 
 
 def aggregator_forward(images: torch.Tensor, pe: dict, specials, frame_blocks: list, global_blocks: list,
-                       patch_start: int = 5, grid_w: int = 37):
+                       patch_start: int = 5):
     """The full aggregator on S frames: DINOv2 front, special tokens, then the
-    frame / global block pairs.  Returns (aggregator input tokens, last frame
-    block output, last global block output), each [S, P, C]."""
+    frame / global block pairs (2-D RoPE over the frames' patch grid, its width
+    = image width / patch).  Returns (aggregator input tokens, last frame block
+    output, last global block output), each [S, P, C]."""
     x = aggregator_tokens(patch_embed_forward(images, pe), specials, 0, patch_start)
+    grid_w = images.shape[-1] // pe["patch"]
     x0 = x
     xf = x
     for fb, gb in zip(frame_blocks, global_blocks):
         xf, x = block_pair_forward(x, fb, gb, patch_start, grid_w)
     return x0, xf, x
+
+
+# ------------------------------------------------------- other frame sizes
+def _aa_bicubic_weights(n_in: int, n_out: int, a: float = -0.5) -> np.ndarray:
+    """[n_out, n_in] resampling matrix of separable antialiased bicubic
+    interpolation: output sample i sits at input coordinate (i + 0.5) * scale,
+    scale = n_in / n_out; the Keys cubic (a = -0.5) is stretched by
+    max(scale, 1) when shrinking, taps are cut to the image and each row is
+    normalised to sum 1 (the published separable-resampling method, as in
+    Pillow's and PyTorch's antialiased resize)."""
+    def cubic(x):
+        x = abs(x)
+        if x < 1.0:
+            return (a + 2.0) * x ** 3 - (a + 3.0) * x ** 2 + 1.0
+        if x < 2.0:
+            return a * x ** 3 - 5.0 * a * x ** 2 + 8.0 * a * x - 4.0 * a
+        return 0.0
+    scale = n_in / n_out
+    fs = max(scale, 1.0)
+    support = 2.0 * fs
+    W = np.zeros((n_out, n_in), np.float64)
+    for i in range(n_out):
+        center = (i + 0.5) * scale
+        lo = max(int(center - support + 0.5), 0)
+        hi = min(int(center + support + 0.5), n_in)
+        w = np.array([cubic((x - center + 0.5) / fs) for x in range(lo, hi)])
+        W[i, lo:hi] = w / w.sum()
+    return W
+
+
+def interpolate_pos_embed(pos_embed, rows: int, cols: int) -> torch.Tensor:
+    """DINOv2's position table [1 + M*M, C] resampled to a rows x cols patch
+    grid (class position kept; patch grid resized as an image, bicubic with
+    antialiasing, in float64 here).  Returns fp32 [1 + rows*cols, C]."""
+    pe = np.asarray(torch.as_tensor(pos_embed).float(), np.float64)
+    M = int(round(math.sqrt(pe.shape[0] - 1)))
+    grid = pe[1:].reshape(M, M, -1)
+    out = np.einsum("ri,ijc,sj->rsc", _aa_bicubic_weights(M, rows), grid, _aa_bicubic_weights(M, cols))
+    return torch.from_numpy(np.concatenate([pe[:1], out.reshape(rows * cols, -1)]).astype(np.float32))

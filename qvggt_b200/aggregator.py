@@ -340,6 +340,9 @@ class PatchEmbed:
     norm_b: torch.Tensor
     patch: int = 14
     k_pad: int = 640
+    # the trained position table [1 + M*M, C] (class position, M x M patch
+    # grid), kept to build `pos` for other frame sizes; None: `pos` only
+    pos_embed: torch.Tensor | None = None
 
 
 class VGGTAggregator:
@@ -348,10 +351,31 @@ class VGGTAggregator:
     patchify -> patch GEMM -> [cls | registers | patches] + pos -> DINOv2 blocks
     -> LayerNorm -> [camera | registers | patch tokens] (first frame of the
     sequence uses its own camera / register tokens) -> 24 frame/global pairs.
+
+    ``img_hw``: the frame size, multiples of the patch size (QVGGT's loader
+    gives 518 wide and at most 518 tall, ``qvggt_b200.frames.crop_size``).  A
+    patch grid other than the position table's is served with the table
+    resampled to it (``frames.token_position_table``); the token count per
+    frame, the 2-D RoPE grid width and the frame attention follow the grid.
     """
 
     def __init__(self, cfg: AggConfig, pe: PatchEmbed, agg_specials: torch.Tensor, frame_blocks, global_blocks,
                  frames_local: int, device, group=None, world: int = 1, rank: int = 0, img_hw=(518, 518)):
+        import dataclasses
+        H, W = img_hw
+        if H <= 0 or W <= 0 or H % pe.patch or W % pe.patch:
+            raise ValueError(f"frame size {img_hw} must be positive multiples of the patch size {pe.patch}")
+        rows, cols = H // pe.patch, W // pe.patch
+        self.n_patch = rows * cols
+        if self.n_patch + cfg.patch_start != cfg.tokens_per_frame or cols != cfg.grid_w:
+            cfg = dataclasses.replace(cfg, tokens_per_frame=self.n_patch + cfg.patch_start, grid_w=cols)
+        if pe.pos.shape[0] != cfg.tokens_per_frame:
+            if pe.pos_embed is None:
+                raise ValueError(f"the position table holds {pe.pos.shape[0] - cfg.patch_start} patches, the "
+                                 f"{H} x {W} frames have {self.n_patch}, and no trained table to resample")
+            from .frames import token_position_table
+            pos = token_position_table(pe.pos_embed, rows, cols, cfg.patch_start)
+            pe = dataclasses.replace(pe, pos=pos.to(pe.pos.device).contiguous())
         self.cfg = cfg
         self.pe = pe
         self.agg_specials = agg_specials            # [2, 5, C]: camera + 4 registers, frame 0 / others
@@ -359,9 +383,6 @@ class VGGTAggregator:
         self.S_local = frames_local
         self.rank = rank
         self.img_hw = img_hw
-        H, W = img_hw
-        self.n_patch = (H // pe.patch) * (W // pe.patch)
-        assert self.n_patch + cfg.patch_start == cfg.tokens_per_frame
         dev = torch.device(device)
         C = cfg.dim
         self.patches = torch.empty(frames_local * self.n_patch, pe.k_pad, dtype=F16, device=dev)

@@ -182,10 +182,12 @@ def _count(sd, prefix: str) -> int:
     return len(idx)
 
 
-def patch_embed_from_state_dict(sd, device, prefix: str = "aggregator.patch_embed", tokens_per_frame: int = 1374,
-                                n_special: int = 5, k_pad: int = 640) -> PatchEmbed:
-    """DINOv2 front.  The positional table must already match the patch grid
-    (37 x 37 for 518 x 518 frames, as VGGT's checkpoints store it)."""
+def patch_embed_from_state_dict(sd, device, prefix: str = "aggregator.patch_embed", n_special: int = 5,
+                                k_pad: int = 640) -> PatchEmbed:
+    """DINOv2 front.  ``pos`` is the per-token table for the trained grid
+    (37 x 37 patches, 518 x 518 frames, as VGGT's checkpoints store it); the
+    trained table is kept as ``pos_embed`` so ``VGGTAggregator`` can resample
+    it for other frame sizes."""
     w = sd[prefix + ".patch_embed.proj.weight"]                       # [C, 3, p, p]
     C, cin, p, _ = w.shape
     kin = cin * p * p
@@ -196,12 +198,8 @@ def patch_embed_from_state_dict(sd, device, prefix: str = "aggregator.patch_embe
     regs = sd[prefix + ".register_tokens"].reshape(1, -1, C)
     if 1 + regs.shape[1] != n_special:
         raise ValueError(f"expected {n_special - 1} register tokens, got {regs.shape[1]}")
-    pos_embed = sd[prefix + ".pos_embed"].reshape(-1, C)                 # [1 + n_patch, C]
-    n_patch = tokens_per_frame - n_special
-    if pos_embed.shape[0] != 1 + n_patch:
-        raise NotImplementedError(f"pos_embed holds {pos_embed.shape[0] - 1} patches, the frames have {n_patch}: "
-                                  "positional interpolation is not built")
-    pos = torch.zeros(tokens_per_frame, C, dtype=F16)
+    pos_embed = sd[prefix + ".pos_embed"].reshape(-1, C)                 # [1 + M*M, C]
+    pos = torch.zeros(pos_embed.shape[0] - 1 + n_special, C, dtype=F16)
     pos[0] = pos_embed[0].to(F16)
     pos[n_special:] = pos_embed[1:].to(F16)
     depth = _count(sd, prefix + ".blocks.")
@@ -209,12 +207,15 @@ def patch_embed_from_state_dict(sd, device, prefix: str = "aggregator.patch_embe
     return PatchEmbed(patch_w=patch_w, patch_b=_t(sd, prefix + ".patch_embed.proj.bias", device, F16).contiguous(),
                       specials=torch.cat([cls, regs], 1).to(F16).to(device).contiguous(), pos=pos.to(device).contiguous(),
                       blocks=blocks, norm_w=_t(sd, prefix + ".norm.weight", device, F16).contiguous(),
-                      norm_b=_t(sd, prefix + ".norm.bias", device, F16).contiguous(), patch=p, k_pad=k_pad)
+                      norm_b=_t(sd, prefix + ".norm.bias", device, F16).contiguous(), patch=p, k_pad=k_pad,
+                      pos_embed=pos_embed.detach().to(F16).cpu().contiguous())
 
 
 def aggregator_from_state_dict(sd, frames_local: int, device, group=None, world: int = 1, rank: int = 0,
-                               group_size: int = 128, cfg: AggConfig | None = None) -> VGGTAggregator:
-    """Build the runtime aggregator for this rank's ``frames_local`` frames."""
+                               group_size: int = 128, cfg: AggConfig | None = None,
+                               img_hw=(518, 518)) -> VGGTAggregator:
+    """Build the runtime aggregator for this rank's ``frames_local`` frames of
+    ``img_hw`` pixels (the position table is resampled for other sizes)."""
     sd = strip_model_prefix(sd)
     depth = _count(sd, "aggregator.frame_blocks.")
     if depth == 0 or depth != _count(sd, "aggregator.global_blocks."):
@@ -229,9 +230,8 @@ def aggregator_from_state_dict(sd, frames_local: int, device, group=None, world:
     cam = sd["aggregator.camera_token"].reshape(2, 1, C)
     reg = sd["aggregator.register_token"].reshape(2, -1, C)
     specials = torch.cat([cam, reg], 1).to(F16).to(device).contiguous()          # [2, 5, C]
-    pe = patch_embed_from_state_dict(sd, device, tokens_per_frame=cfg.tokens_per_frame,
-                                     n_special=cfg.patch_start)
-    return VGGTAggregator(cfg, pe, specials, frame, glob, frames_local, device, group, world, rank)
+    pe = patch_embed_from_state_dict(sd, device, n_special=cfg.patch_start)
+    return VGGTAggregator(cfg, pe, specials, frame, glob, frames_local, device, group, world, rank, img_hw=img_hw)
 
 
 def camera_trunk_from_state_dict(sd, device, group_size: int = 128, prefix: str = "camera_head.trunk"):

@@ -95,15 +95,18 @@ def random_patch_embed(cfg: AggConfig, gen: torch.Generator, device, depth: int 
     pos = torch.zeros(cfg.tokens_per_frame, C, device=device)
     pos[0] = r(C) * 0.02
     pos[cfg.patch_start:] = r(cfg.tokens_per_frame - cfg.patch_start, C) * 0.02
+    # the trained-table form [1 + M*M, C]: class position, then the patch grid
+    pos_embed = torch.cat([pos[:1], pos[cfg.patch_start:]]).to(F16)
     blocks = [random_block(cfg, gen, device, kind="f16", layer_scale=layer_scale, qk_norm=False) for _ in range(depth)]
     return PatchEmbed(patch_w=w.to(F16).contiguous(), patch_b=(r(C) * 0.01).to(F16),
                       specials=(r(1, cfg.patch_start, C) * 0.02).to(F16).contiguous(), pos=pos.to(F16).contiguous(),
                       blocks=blocks, norm_w=(1 + 0.1 * r(C)).to(F16), norm_b=(0.1 * r(C)).to(F16), patch=patch,
-                      k_pad=k_pad)
+                      k_pad=k_pad, pos_embed=pos_embed.cpu())
 
 
 def random_vggt_aggregator(cfg: AggConfig, seed: int, device, frames_local: int, group=None, world: int = 1,
-                           rank: int = 0, pe_depth: int = 24, kind: str = "w4", pe_layer_scale: float = 1e-5):
+                           rank: int = 0, pe_depth: int = 24, kind: str = "w4", pe_layer_scale: float = 1e-5,
+                           img_hw=(518, 518)):
     """Full synthetic VGGT-1B aggregator: DINOv2 front in fp16 + ``cfg.depth``
     frame/global pairs with ``kind`` linears ("w4": BASELINE config 2, "w8":
     the W8A8 chain of config 3), identical on every rank."""
@@ -113,7 +116,7 @@ def random_vggt_aggregator(cfg: AggConfig, seed: int, device, frames_local: int,
     specials = (torch.randn(2, cfg.patch_start, cfg.dim, generator=gen, device=device) * 0.02).to(F16).contiguous()
     frame = [random_block(cfg, gen, device, kind) for _ in range(cfg.depth)]
     glob = [random_block(cfg, gen, device, kind) for _ in range(cfg.depth)]
-    return VGGTAggregator(cfg, pe, specials, frame, glob, frames_local, device, group, world, rank)
+    return VGGTAggregator(cfg, pe, specials, frame, glob, frames_local, device, group, world, rank, img_hw=img_hw)
 
 
 def synthetic_images(S: int, seed: int, H: int = 518, W: int = 518) -> torch.Tensor:

@@ -119,3 +119,32 @@ def test_patchify_matches_oracle_bit_for_bit():
     ref = om.patchify(images, 14)
     assert torch.equal(got[:, :588], ref)
     assert not got[:, 588:].any()
+
+
+def test_vggt_aggregator_landscape_frames_match_oracle():
+    """Frames of 392 x 518 (QVGGT's crop of a 4:3 image: 28 x 37 patches,
+    1,041 tokens per frame): the position table resampled from the trained
+    37 x 37 one, the per-frame attention, the 2-D RoPE grid and the global
+    attention follow the grid; against the oracle with its own resampling of
+    the table."""
+    from qvggt_b200.aggregator import AggConfig
+    from qvggt_b200.synthetic import random_vggt_aggregator, synthetic_images
+    H, W = 392, 518
+    cfg = AggConfig(depth=1, layer_scale=0.2)
+    S = 2
+    agg = random_vggt_aggregator(cfg, 29, DEV, S, pe_depth=1, pe_layer_scale=0.3, img_hw=(H, W))
+    assert agg.cfg.tokens_per_frame == 5 + 28 * 37 and agg.cfg.grid_w == 37
+    images = synthetic_images(S, 12, H, W)
+    tokens = agg.embed(images.to(DEV)).clone().cpu()
+    fr, gl = agg.forward(images.to(DEV))[-1]
+    pe = _oracle_patch_embed(agg.pe, agg.cfg)
+    table = om.interpolate_pos_embed(agg.pe.pos_embed, 28, 37)
+    pe["pos_cls"], pe["pos_patch"] = table[0].half(), table[1:].half()
+    x0, ref_f, ref_g = om.aggregator_forward(images, pe, agg.agg_specials.cpu(),
+                                             [_oracle_block(b) for b in agg.runner.frame_blocks],
+                                             [_oracle_block(b) for b in agg.runner.global_blocks])
+    P, C = agg.cfg.tokens_per_frame, agg.cfg.dim
+    assert awq.rel_l2(tokens[:, 5:], x0[:, 5:]) <= 2e-2
+    assert awq.rel_l2(fr.view(S, P, C).cpu(), ref_f) <= 2e-2
+    assert awq.rel_l2(gl.view(S, P, C).cpu(), ref_g) <= 2e-2
+    assert awq.rel_l2(gl.view(S, P, C).cpu().float() - tokens.float(), ref_g.float() - x0.float()) <= 5e-2
