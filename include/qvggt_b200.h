@@ -305,6 +305,27 @@ int qvggt_assemble_tokens(const void* src, int64_t src_rows_per_frame, int64_t s
  * gemm_cuda.cu:1154-1232). */
 int qvggt_set_gemm_config(int32_t cfg);
 
+/* ------------------------------------------------------- post-processing */
+
+/* Camera matrices from VGGT's pose encoding "absT_quaR_FoV": pose_enc fp32
+ * [n, 9] = (t, quaternion x y z w, fov_h, fov_w) -> extrinsics fp32 [n, 3, 4] =
+ * [R | t] and, when `intrinsics` is not NULL, intrinsics fp32 [n, 3, 3]
+ * (fx = (w/2) / tan(fov_w/2), fy = (h/2) / tan(fov_h/2), fields of view
+ * clamped to [1e-6, pi - 1e-6], focal lengths to [1, 1e6], principal point
+ * (w/2, h/2)).  Replaces qvggt/common/pose_enc.py:7-65
+ * (pose_encoding_to_extri_intri) and rotation.py:4-25 (quat_to_mat). */
+int qvggt_pose_encoding_to_extri_intri(const float* pose_enc, int64_t n, int32_t image_h, int32_t image_w,
+                                        float* extrinsics, float* intrinsics, void* stream);
+
+/* World points from depth maps: depth fp32 [S, H, W] (16-byte aligned),
+ * extrinsics fp32 [S, 3, 4], intrinsics fp32 [S, 3, 3] -> world_points fp32
+ * [S, H, W, 3] (16-byte aligned) = R^T (cam - t) with cam = ((u - cu) d / fu,
+ * (v - cv) d / fv, d), fu and fv floored at 1e-6; every pixel is converted
+ * (no mask), as in the reference.  Replaces qvggt/common/geometry.py:43-96
+ * (unproject_depth_map_to_point_map, computed there in numpy on the host). */
+int qvggt_unproject_depth(const float* depth, int64_t S, int32_t H, int32_t W, const float* extrinsics,
+                          const float* intrinsics, float* world_points, void* stream);
+
 /* ------------------------------------------------------------- self-test */
 
 /* Runs one kernel whose bounded wait waits on an mbarrier nothing arrives on;

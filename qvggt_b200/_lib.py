@@ -52,6 +52,8 @@ SIGNATURES = {
     "qvggt_selftest_wait_timeout": [u64, u32p],
     "qvggt_patchify": [vp, vp, i64, i32, i32, i32, i32, C.POINTER(f32), C.POINTER(f32), vp],
     "qvggt_assemble_tokens": [vp, i64, i64, vp, i32, i32, vp, vp, i64, i32, i32, i64, vp],
+    "qvggt_pose_encoding_to_extri_intri": [vp, i64, i32, i32, vp, vp, vp],
+    "qvggt_unproject_depth": [vp, i64, i32, i32, vp, vp, vp, vp],
 }
 _RESTYPES = {"qvggt_last_error": C.c_char_p, "qvggt_launch_count": C.c_uint64}
 
