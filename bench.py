@@ -273,7 +273,8 @@ def check_against_one_gpu(model, cfg, args, ws, rank, dev, img_dev, S, S_local):
     res = None
     if rank == 0:
         full = torch.cat(parts).float()
-        one = random_vggt_aggregator(cfg, seed=1234, device=dev, frames_local=S, pe_depth=args.depth)
+        one = random_vggt_aggregator(cfg, seed=1234, device=dev, frames_local=S, pe_depth=args.depth,
+                                     kind=args.linears)
         ref = one.forward(synthetic_images(S, seed=args.seed).to(dev))[-1][1].float()
         res = {"rel_l2_vs_1gpu": float((full - ref).norm() / ref.norm()), "frames": S,
                "what": "last pair's global-block output, all ranks gathered, vs a one-GPU forward on the same seeds"}
@@ -290,6 +291,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--frames", type=int, default=32)
     ap.add_argument("--seed", type=int, default=0, help="image seed (BASELINE config 2: 0, config 4: 1)")
+    ap.add_argument("--linears", default="w4", choices=["w4", "w8"],
+                    help="aggregator linears: w4 = W4A16 g128 (configs 2 and 4), w8 = W8A8 (config 3, --frames 64)")
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--depth", type=int, default=24)
@@ -317,7 +320,7 @@ def main():
     cfg = AggConfig(depth=args.depth)
     group = torch.distributed.group.WORLD if ws > 1 else None
     model = random_vggt_aggregator(cfg, seed=1234, device=dev, frames_local=S_local, group=group, world=ws,
-                                   rank=rank, pe_depth=args.depth)
+                                   rank=rank, pe_depth=args.depth, kind=args.linears)
     if args.no_overlap_kv:
         model.runner.overlap_kv = False
     images = synthetic_images(S, seed=args.seed)[rank * S_local:(rank + 1) * S_local].contiguous()
@@ -378,7 +381,7 @@ def main():
     peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
 
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and args.linears == "w4":
         v, cores, sample = cpu_oracle_sample(S)
         cpu = {"value": v, "unit": "frames/s", "cores": cores, "kind": "port", "sample": sample}
 
@@ -387,12 +390,13 @@ def main():
     if rank == 0:
         clocks = clk.summary()
         line = {
-            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": ws, "steps": args.steps,
+            "metric": METRIC if args.linears == "w4" else METRIC.replace("W4A16", "W8A8"), "value": value, "unit": "frames/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * t_dev / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": f"synthetic (U[0,1] 518x518 frames, seed {args.seed}; random-init VGGT-1B weights quantised "
-                    f"W4A16 g128)",
-            "config": {"workload": f"VGGT-1B aggregator forward (DINOv2 ViT-L/14 fp16 front + {args.depth} W4A16 "
+                    f"{'W4A16 g128' if args.linears == 'w4' else 'W8A8 per-channel / per-token'})",
+            "config": {"workload": f"VGGT-1B aggregator forward (DINOv2 ViT-L/14 fp16 front + {args.depth} "
+                                   f"{'W4A16' if args.linears == 'w4' else 'W8A8'} "
                                    f"frame/global pairs), S={S} frames, 518x518",
                        "frames": S, "frames_per_gpu": S_local, "tokens_per_frame": cfg.tokens_per_frame,
                        "parallelism": f"frame-sharded x{ws}, NCCL K/V all-gather per global block",
