@@ -121,8 +121,12 @@ def dist_init():
     if ws > 1:
         import datetime
         torch.cuda.set_device(local)
+        # NCCL's kernels run on a high-priority stream, so the K/V all-gather
+        # gets SMs as soon as CTAs of the attention it overlaps retire
+        opts = torch.distributed.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=torch.device("cuda", local))
+                                             device_id=torch.device("cuda", local), pg_options=opts)
     else:
         torch.cuda.set_device(local)
     return ws, rank, local
