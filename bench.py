@@ -300,6 +300,8 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--depth", type=int, default=24)
+    ap.add_argument("--graph", action="store_true",
+                    help="one GPU: also time the forward captured once in a CUDA graph and replayed")
     ap.add_argument("--no-overlap-kv", action="store_true",
                     help="N > 1: attend only after the whole K/V all-gather (no local-keys pass during it)")
     args = ap.parse_args()
@@ -362,6 +364,31 @@ def main():
     breakdown = step_breakdown(ws, model, args.steps, t_dev, attn_ms, wait_ms)
     parity = check_against_one_gpu(model, cfg, args, ws, rank, dev, img_dev, S, S_local) if ws > 1 else None
 
+    # ---- one GPU: the same forward captured in a CUDA graph, replayed
+    graph = None
+    if args.graph and ws == 1:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            model.forward(img_dev)
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            model.forward(img_dev)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e4.record()
+        for _ in range(args.steps):
+            g.replay()
+        e5.record()
+        torch.cuda.synchronize()
+        t_g = e4.elapsed_time(e5) / 1000.0
+        graph = {"value": S * args.steps / t_g, "ms_per_step": 1000.0 * t_g / args.steps,
+                 "what": "the forward captured once in a CUDA graph, replayed K times"}
+        del g
+
     # ---- end to end through the public API (host buffers)
     for _ in range(max(1, args.warmup // 2)):
         model.infer(img_host, out_host)
@@ -419,6 +446,7 @@ def main():
             "cpu_baseline": cpu,
             "breakdown": breakdown,
             "parity": parity,
+            "graph": graph,
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
