@@ -63,6 +63,16 @@ int qvggt_w4a16_gemm(const void* in_feats, const void* qweight, const void* scal
                      const void* bias, void* out, int64_t M, int64_t N, int64_t K, int64_t gpad,
                      int32_t group_size, void* stream);
 
+/* qvggt_w4a16_gemm with bf16 in_feats, scales, scaled_zeros, bias and out
+ * (same qweight).  Dequantisation w = q * s + sz in one bf16x2 fma, bf16
+ * operands on the tensor cores, fp32 accumulation, out = bf16(acc) (with a
+ * bias: bf16(bf16(acc) + bias)).  Replaces the bf16 instantiation of
+ * gemm_forward_cuda_new (E/quantization_new/gemm/gemm_cuda.cu:1146 dispatches
+ * nv_bfloat16 through the same kernels; dequantize.cuh:53-90). */
+int qvggt_w4a16_gemm_bf16(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                          const void* bias, void* out, int64_t M, int64_t N, int64_t K, int64_t gpad,
+                          int32_t group_size, void* stream);
+
 /* Same GEMM with a fused epilogue for the VGGT block:
  *   act == 1: out = gelu_erf(half(half(acc) + bias))          (fc1 -> GELU)
  *   resid != NULL: resid[M, ldr] += half(half(half(acc)+bias) * gamma)
@@ -100,7 +110,9 @@ int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, c
 /* Small-M linear (1 <= M <= 256 rows; N % 128 == 0, K % 64 == 0): the same
  * result and epilogues as qvggt_w4a16_linear_ex (weight_kind 0: AWQ int4
  * qweight/scales/scaled_zeros/gpad/group_size) or qvggt_f16_linear_ex
- * (weight_kind 1: fp16 weight [N, K] in `weight`, scales ignored), computed
+ * (weight_kind 1: fp16 weight [N, K] in `weight`, scales ignored), or
+ * qvggt_w4a16_gemm_bf16 (weight_kind 2: AWQ int4 with bf16 activations,
+ * scales, bias and output; act = 0 and resid = NULL only), computed
  * with the rows as the tensor-core N dimension and K split across the CTAs
  * of a thread-block cluster (partials summed on chip in a fixed order; no
  * workspace).  Replaces the small-M path of gemm_forward_cuda_new,
@@ -125,6 +137,15 @@ int qvggt_small_linear_plan(int32_t weight_kind, int64_t M, int64_t N, int64_t K
 int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
                      const void* bias, void* out, int64_t m, int64_t N, int64_t K, int64_t gpad,
                      int32_t group_size, void* stream);
+
+/* qvggt_w4a16_gemv with bf16 in_feats, scales, scaled_zeros, bias and out:
+ * bf16 dequantisation as qvggt_w4a16_gemm_bf16, products summed in fp32,
+ * out = bf16(sum) (+ bias).  Replaces the bf16 instantiation of
+ * gemv_forward_cuda_new (E/quantization_new/gemv/gemv_cuda.cu:210-217, 59,
+ * 130-133: the reference sums in bf16). */
+int qvggt_w4a16_gemv_bf16(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                          const void* bias, void* out, int64_t m, int64_t N, int64_t K, int64_t gpad,
+                          int32_t group_size, void* stream);
 
 /* ----------------------------------------------------------------- W8A8 */
 

@@ -130,6 +130,83 @@ def dequantize(qweight, scales_t, szeros_t, group_size: int, K: int | None = Non
     return w.astype(np.float16)
 
 
+def bf16_round(x) -> np.ndarray:
+    """Round float64 values to bf16 (round to nearest even), once; returned as
+    float32 (every bf16 is a float32).  The float64 significand is rounded to
+    bf16's 8 bits directly, so no double rounding through float32.  Normal
+    bf16 range only (|x| >= 2^-126 or 0), which the tests' data stay in."""
+    x = np.ascontiguousarray(np.asarray(x, dtype=np.float64))
+    nz = x[x != 0]
+    assert nz.size == 0 or np.abs(nz).min() >= 2.0 ** -126, "bf16 subnormal range not restated"
+    b = x.view(np.uint64)
+    lsb = (b >> np.uint64(45)) & np.uint64(1)
+    r = (b + np.uint64((1 << 44) - 1) + lsb) & ~np.uint64((1 << 45) - 1)
+    return r.view(np.float64).astype(np.float32)
+
+
+def bf16_bits(x) -> np.ndarray:
+    """uint16 bit patterns of bf16-representable float32 values."""
+    return (np.ascontiguousarray(np.asarray(x, dtype=np.float32)).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(b) -> np.ndarray:
+    return (np.asarray(b).astype(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def dequantize_bf16(qweight, scales_t, szeros_t, group_size: int, K: int | None = None) -> np.ndarray:
+    """Bit-exact bf16 dequantised weight [N, K] (as float32 values).
+
+    The bf16 form of ``dequantize_s4_to_fp16x2`` (``dequantize.cuh:53-90``)
+    gives the exact bf16 integer q (128 + q minus 128), and the kernels apply
+    ``__hfma2(q, s, sz)`` on ``nv_bfloat162`` (``gemm/gemm_cuda.cu:906-915``,
+    ``gemv/gemv_cuda.cu:130-133``): one fused multiply-add rounded once to
+    bf16.  scales_t / szeros_t hold bf16 values (float32 arrays or bf16
+    tensors); q*s + sz is exact in float64.
+    """
+    q = unpack_intweight(np.asarray(qweight))
+    N, Kq = q.shape
+    K = Kq if K is None else K
+    G = group_size if group_size != -1 else K
+    as64 = lambda t: (t.float().numpy() if isinstance(t, torch.Tensor) else np.asarray(t, np.float32)).astype(np.float64)
+    s, z = as64(scales_t), as64(szeros_t)
+    g = np.arange(K) // G
+    return bf16_round(q.astype(np.float64) * s[g, :].T + z[g, :].T)
+
+
+def w4a16_linear_bf16(x, qweight, scales_t, szeros_t, group_size: int = 128, bias=None) -> np.ndarray:
+    """float64-accumulated y = x . deq_bf16(W)^T (+ bf16(y) + bias when a bias
+    is given, the order of the kernels' epilogue), float64 [.., N].  x, the
+    scales and the bias hold bf16 values."""
+    xa = (x.float().numpy() if isinstance(x, torch.Tensor) else np.asarray(x, np.float32)).astype(np.float64)
+    K = xa.shape[-1]
+    w = dequantize_bf16(qweight, scales_t, szeros_t, group_size, K).astype(np.float64)
+    y = xa.reshape(-1, K) @ w.T
+    if bias is not None:
+        b = (bias.float().numpy() if isinstance(bias, torch.Tensor) else np.asarray(bias, np.float32))
+        y = bf16_round(y).astype(np.float64) + b.astype(np.float64)
+    return y.reshape(*xa.shape[:-1], w.shape[0])
+
+
+def make_quantized_linear_bf16(N: int, K: int, group_size: int = 128, seed: int = 0, bias: bool = True):
+    """:func:`make_quantized_linear` with bf16 scales, scaled zeros and bias
+    (float32 arrays of bf16 values), the way the reference's ``from_linear``
+    builds them for a bf16 model: scaled zeros = bf16(-(s * z)) with s in bf16
+    (``qmodule.py:302-306``)."""
+    G = group_size if group_size != -1 else K
+    rng = np.random.default_rng(seed)
+    q = rng.integers(0, 16, size=(N, K), dtype=np.int32)
+    zeros = rng.integers(0, 16, size=(N, K // G)).astype(np.float64)
+    scales = bf16_round(np.maximum(np.abs(rng.standard_normal((N, K // G))) * 0.02, 1e-4))
+    gpad = calculate_zeros_width(K, group_size) * 8
+    st = np.zeros((gpad, N), dtype=np.float32)
+    st[: K // G] = scales.T
+    szt = np.zeros((gpad, N), dtype=np.float32)
+    szt[: K // G] = bf16_round(-(scales.astype(np.float64) * zeros)).T
+    b = bf16_round(rng.standard_normal(N) * 0.01) if bias else None
+    return dict(qweight=pack_intweight(q), scales=st, scaled_zeros=szt, bias=b, q=q, zeros=zeros,
+                scales_ng=scales, group_size=group_size)
+
+
 def _f16(x):
     return x.to(torch.float16) if isinstance(x, torch.Tensor) else torch.from_numpy(np.asarray(x, dtype=np.float16))
 

@@ -26,11 +26,13 @@ SIGNATURES = {
     "qvggt_set_gemm_config": [i32],
     "qvggt_launch_count": [],
     "qvggt_w4a16_gemm": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
+    "qvggt_w4a16_gemm_bf16": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
     "qvggt_w4a16_linear_ex": [vp, i64, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, i64, vp, vp],
     "qvggt_f16_linear_ex": [vp, i64, vp, vp, vp, i64, i64, i64, i64, i32, vp, i64, vp, vp],
     "qvggt_qkv_rope_linear": [vp, i32, vp, vp, vp, i64, i32, vp, vp, vp, i64, i64, i32, i64, i32, i32, i32, vp, vp,
                               i32, i32, vp, vp, vp, vp, f32, vp],
     "qvggt_w4a16_gemv": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
+    "qvggt_w4a16_gemv_bf16": [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp],
     "qvggt_small_linear": [i32, vp, i64, vp, vp, vp, i64, i32, vp, vp, i64, i64, i64, i64, i32, vp, i64, vp, vp],
     "qvggt_small_linear_plan": [i32, i64, i64, i64, C.POINTER(i32)],
     "qvggt_w8a8_gemm": [vp, vp, vp, vp, vp, vp, i64, i64, i64, vp],

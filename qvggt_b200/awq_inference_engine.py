@@ -68,12 +68,12 @@ def _check_shape(name, cond: bool, what: str):
         raise ValueError(f"{name}: {what}")
 
 
-def _check_w4_weights(name, qweight, scales, scaled_zeros, K: int, group_size: int):
-    """qweight int16 [N/4, K]; scales / scaled_zeros fp16 [gpad, N] with at
+def _check_w4_weights(name, qweight, scales, scaled_zeros, K: int, group_size: int, dtype=torch.float16):
+    """qweight int16 [N/4, K]; scales / scaled_zeros ``dtype`` [gpad, N] with at
     least K / group_size group rows (the kernels read that many)."""
     _check_dtype(name, qweight, torch.int16)
-    _check_dtype(name, scales, torch.float16)
-    _check_dtype(name, scaled_zeros, torch.float16)
+    _check_dtype(name, scales, dtype)
+    _check_dtype(name, scaled_zeros, dtype)
     _check_shape(name, qweight.dim() == 2 and qweight.shape[1] == K,
                  f"qweight {tuple(qweight.shape)} must be [N/4, K={K}]")
     N = qweight.shape[0] * 4
@@ -122,34 +122,40 @@ class _Dev:
 def gemm_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, group_size: int = 128):
     """C = in_feats . deq(qweight)^T (``gemm_cuda.cu:1125-1235``).
 
-    in_feats fp16 [..., K]; qweight int16 [N/4, K]; scales / scaled_zeros fp16
-    [gpad, N].  Returns a new fp16 tensor [..., N].  The reference fixes the
-    group size at 128; it is a keyword here for other multiples of 64.
+    in_feats fp16 or bf16 [..., K]; qweight int16 [N/4, K]; scales /
+    scaled_zeros [gpad, N] of the same dtype as in_feats (the reference's
+    TORCH_CHECKs, ``gemm_cuda.cu:1143-1146``).  Returns a new tensor [..., N]
+    of that dtype.  The reference fixes the group size at 128; it is a
+    keyword here for other multiples of 64.
     """
     name = "gemm_forward_cuda_new"
     dev = _check_cuda(name, in_feats, qweight, scales, scaled_zeros)
-    _check_dtype(name, in_feats, torch.float16)
+    _check_dtype(name, in_feats, torch.float16, torch.bfloat16)
+    bf16 = in_feats.dtype == torch.bfloat16
     _contig(name, in_feats, qweight, scales, scaled_zeros)
     K = in_feats.shape[-1]
-    N = _check_w4_weights(name, qweight, scales, scaled_zeros, K, group_size)
+    N = _check_w4_weights(name, qweight, scales, scaled_zeros, K, group_size, in_feats.dtype)
     M = in_feats.numel() // K
     out = torch.empty(*in_feats.shape[:-1], N, dtype=in_feats.dtype, device=dev)
     with _Dev(dev):
         if 1 <= M <= SMALL_M_MAX:
-            _small_linear(0, in_feats, qweight, scales, scaled_zeros, group_size, None, out, M, N, K, 0, None, None)
+            _small_linear(2 if bf16 else 0, in_feats, qweight, scales, scaled_zeros, group_size, None, out, M, N, K,
+                          0, None, None)
         else:
-            _lib.call("qvggt_w4a16_gemm", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
-                      _ptr(out), M, N, K, scales.shape[0], group_size, _stream(in_feats))
+            _lib.call("qvggt_w4a16_gemm_bf16" if bf16 else "qvggt_w4a16_gemm", _ptr(in_feats), _ptr(qweight),
+                      _ptr(scales), _ptr(scaled_zeros), None, _ptr(out), M, N, K, scales.shape[0], group_size,
+                      _stream(in_feats))
     return out
 
 
 def gemv_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, m: int, n: int, k: int, group_size: int):
-    """y = in_feats . deq(qweight)^T for m <= 16 rows (``gemv_cuda.cu:197-281``)."""
+    """y = in_feats . deq(qweight)^T for m <= 16 rows (``gemv_cuda.cu:197-281``);
+    fp16 or bf16 in_feats, with scales / scaled_zeros of the same dtype."""
     name = "gemv_forward_cuda_new"
     dev = _check_cuda(name, in_feats, qweight, scales, scaled_zeros)
-    _check_dtype(name, in_feats, torch.float16)
-    _check_dtype(name, scales, torch.float16)
-    _check_dtype(name, scaled_zeros, torch.float16)
+    _check_dtype(name, in_feats, torch.float16, torch.bfloat16)
+    _check_dtype(name, scales, in_feats.dtype)
+    _check_dtype(name, scaled_zeros, in_feats.dtype)
     _contig(name, in_feats, qweight, scales, scaled_zeros)
     if not (1 <= m <= 16):
         raise RuntimeError("Unsupported batch size for gemv kernel.")
@@ -157,11 +163,12 @@ def gemv_forward_cuda_new(in_feats, qweight, scales, scaled_zeros, m: int, n: in
         raise RuntimeError("Unsupported group size for gemv kernel.")
     _check_shape(name, in_feats.shape[-1] == k and in_feats.numel() >= m * k,
                  f"in_feats {tuple(in_feats.shape)} must hold m={m} rows of k={k}")
-    _check_shape(name, _check_w4_weights(name, qweight, scales, scaled_zeros, k, group_size) == n,
+    _check_shape(name, _check_w4_weights(name, qweight, scales, scaled_zeros, k, group_size, in_feats.dtype) == n,
                  f"qweight {tuple(qweight.shape)} does not give n={n} channels")
     out = torch.empty(*in_feats.shape[:-1], n, dtype=in_feats.dtype, device=dev)
+    entry = "qvggt_w4a16_gemv_bf16" if in_feats.dtype == torch.bfloat16 else "qvggt_w4a16_gemv"
     with _Dev(dev):
-        _lib.call("qvggt_w4a16_gemv", _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
+        _lib.call(entry, _ptr(in_feats), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), None,
                   _ptr(out), m, n, k, scales.shape[0], group_size, _stream(in_feats))
     return out
 
@@ -173,10 +180,14 @@ def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 
     ``residual += half(y * gamma)`` (returns ``residual``).  Up to
     ``GEMV_M_MAX`` rows (plain / bias epilogue) use the GEMV kernel, up to
     ``SMALL_M_MAX`` rows the split-K small-M kernel, more the persistent
-    tcgen05 GEMM."""
+    tcgen05 GEMM.  bf16 ``x`` (with bf16 scales, zeros, bias): the plain /
+    bias linear only, ``bf16(bf16(x.W^T) + bias)``."""
     name = "w4a16_linear"
     dev = _check_cuda(name, x, qweight, scales, scaled_zeros, bias, residual, gamma, out)
-    _check_dtype(name, x, torch.float16)
+    _check_dtype(name, x, torch.float16, torch.bfloat16)
+    if x.dtype == torch.bfloat16:
+        return _w4a16_linear_bf16(name, dev, x, qweight, scales, scaled_zeros, bias, group_size, act, residual,
+                                  out)
     _contig(name, x, qweight, scales, scaled_zeros, bias, gamma)
     K = x.shape[-1]
     N = _check_w4_weights(name, qweight, scales, scaled_zeros, K, group_size)
@@ -200,6 +211,38 @@ def w4a16_linear(x, qweight, scales, scaled_zeros, bias=None, group_size: int = 
             _lib.call("qvggt_w4a16_linear_ex", _ptr(x), K, _ptr(qweight), _ptr(scales), _ptr(scaled_zeros),
                       _ptr(bias), _ptr(out), N, M, N, K, scales.shape[0], group_size, 1 if act == "gelu" else 0,
                       _ptr(residual), N if residual is not None else 0, _ptr(gamma), _stream(x))
+    return out
+
+
+def _w4a16_linear_bf16(name, dev, x, qweight, scales, scaled_zeros, bias, group_size, act, residual, out):
+    """bf16 form of :func:`w4a16_linear` (the reference's bf16 instantiation of
+    gemv_forward_cuda_new / gemm_forward_cuda_new plus WQLinear's bias add)."""
+    if act is not None or residual is not None:
+        raise NotImplementedError(f"{name}: bf16 activations take the plain / bias linear only")
+    _contig(name, x, qweight, scales, scaled_zeros, bias)
+    K = x.shape[-1]
+    N = _check_w4_weights(name, qweight, scales, scaled_zeros, K, group_size, torch.bfloat16)
+    M = x.numel() // K
+    if bias is not None:
+        _check_dtype(name, bias, torch.bfloat16)
+        _check_shape(name, bias.numel() >= N, f"bias has {bias.numel()} entries, needs {N}")
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=dev)
+    else:
+        _check_dtype(name, out, torch.bfloat16)
+        _contig(name, out)
+        _check_shape(name, out.shape[-1] == N and out.numel() == M * N, f"out {tuple(out.shape)} must hold {M} rows of N={N}")
+    if M == 0:
+        return out
+    with _Dev(dev):
+        if M <= GEMV_M_MAX:
+            _lib.call("qvggt_w4a16_gemv_bf16", _ptr(x), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), _ptr(bias),
+                      _ptr(out), M, N, K, scales.shape[0], group_size, _stream(x))
+        elif M <= SMALL_M_MAX:
+            _small_linear(2, x, qweight, scales, scaled_zeros, group_size, bias, out, M, N, K, 0, None, None)
+        else:
+            _lib.call("qvggt_w4a16_gemm_bf16", _ptr(x), _ptr(qweight), _ptr(scales), _ptr(scaled_zeros), _ptr(bias),
+                      _ptr(out), M, N, K, scales.shape[0], group_size, _stream(x))
     return out
 
 

@@ -184,6 +184,20 @@ int qvggt_w4a16_gemm(const void* in_feats, const void* qweight, const void* scal
                                0, nullptr, 0, nullptr, stream);
 }
 
+int qvggt_w4a16_gemm_bf16(const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                          const void* bias, void* out, int64_t M, int64_t N, int64_t K, int64_t gpad,
+                          int32_t group_size, void* stream) {
+  GemmLaunch L;
+  L.mode = B_W4BF;
+  L.epi = EPI_STORE;
+  L.a = in_feats; L.lda = K; L.b = qweight; L.scales = scales; L.zeros = scaled_zeros; L.gpad = gpad;
+  L.group_size = group_size; L.bias = bias; L.out = out; L.ldo = N;
+  L.M = M; L.N = N; L.K = K; L.stream = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(L);
+  if (rc == QVGGT_OK && M > 0) count_launch(1);
+  return rc;
+}
+
 int qvggt_w4a16_linear_ex(const void* in_feats, int64_t lda, const void* qweight, const void* scales,
                           const void* scaled_zeros, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
                           int64_t K, int64_t gpad, int32_t group_size, int32_t act, const void* resid,
@@ -242,11 +256,16 @@ int qvggt_f16_linear_ex(const void* in_feats, int64_t lda, const void* weight, c
   return rc;
 }
 
+// weight_kind of qvggt_small_linear -> GemmMode (-1: invalid)
+static int small_mode(int32_t weight_kind) {
+  return weight_kind == 0 ? B_W4 : weight_kind == 1 ? B_F16 : weight_kind == 2 ? B_W4BF : -1;
+}
+
 int qvggt_small_linear_plan(int32_t weight_kind, int64_t M, int64_t N, int64_t K, int32_t* info) {
   if (!info) return set_error(QVGGT_ERR_INVALID, "small_linear_plan: info is null");
-  if (weight_kind != 0 && weight_kind != 1) return set_error(QVGGT_ERR_INVALID, "small_linear: weight_kind");
+  if (small_mode(weight_kind) < 0) return set_error(QVGGT_ERR_INVALID, "small_linear: weight_kind");
   SmallPlan P;
-  int rc = gemm_small_plan(weight_kind == 0 ? B_W4 : B_F16, M, N, K, 0, &P);
+  int rc = gemm_small_plan(small_mode(weight_kind), M, N, K, 0, &P);
   if (rc) return rc;
   info[0] = P.mt;
   info[1] = P.splits;
@@ -260,14 +279,15 @@ int qvggt_small_linear(int32_t weight_kind, const void* in_feats, int64_t lda, c
                        const void* scaled_zeros, int64_t gpad, int32_t group_size, const void* bias, void* out,
                        int64_t ldo, int64_t M, int64_t N, int64_t K, int32_t act, const void* resid, int64_t ldr,
                        const void* gamma, void* stream) {
-  if (weight_kind != 0 && weight_kind != 1) return set_error(QVGGT_ERR_INVALID, "small_linear: weight_kind");
+  const int mode = small_mode(weight_kind);
+  if (mode < 0) return set_error(QVGGT_ERR_INVALID, "small_linear: weight_kind");
   if (resid && act) return set_error(QVGGT_ERR_INVALID, "act and residual are exclusive");
   if (resid && resid != out) return set_error(QVGGT_ERR_INVALID, "residual epilogue updates in place: out == resid");
   SmallPlan P;
-  int rc = gemm_small_plan(weight_kind == 0 ? B_W4 : B_F16, M, N, K, 0, &P);
+  int rc = gemm_small_plan(mode, M, N, K, 0, &P);
   if (rc) return rc;
   GemmLaunch L;
-  L.mode = weight_kind == 0 ? B_W4 : B_F16;
+  L.mode = mode;
   L.epi = resid ? EPI_RESID : (act == 1 ? EPI_GELU : EPI_STORE);
   L.a = in_feats; L.lda = lda; L.b = weight; L.scales = scales; L.zeros = scaled_zeros; L.gpad = gpad;
   L.group_size = group_size; L.bias = bias; L.out = out; L.ldo = ldo; L.resid = resid; L.ldr = ldr;

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -206,9 +207,11 @@ __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint
 // Instruction descriptor, kind::f16: fp32 accumulate, fp16 A/B.
 // bits: [4,6) D fmt (1 = f32), [7,10) A fmt (0 = f16), [10,13) B fmt,
 // 15 A major (1 = MN), 16 B major, [17,23) N>>3, [24,29) M>>4.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major = false, bool b_mn_major = false) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major = false, bool b_mn_major = false,
+                                                 bool bf16 = false) {
+  // A / B format fields (bits 7-9, 10-12): 0 = f16, 1 = bf16 (both the same type)
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 // Instruction descriptor, kind::i8: s32 accumulate, signed A/B.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
@@ -443,6 +446,15 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t u) {
   return __half22float2(h);
 }
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_bf162(uint32_t u) {
+  // a bf16 is the high half of its fp32: widening is a shift
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

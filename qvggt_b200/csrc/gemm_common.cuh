@@ -128,6 +128,28 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + e
 // Epilogue for 16 consecutive columns of one row held as fp32 (or s32) bits.
 template <int MODE>
 __device__ __forceinline__ void epilogue16(const GemmArgs& g, int row, int col, const uint32_t (&r)[16]) {
+  if constexpr (MODE == B_W4BF) {
+    // bf16 store: y = bf16(acc), or bf16(bf16(acc) + bias) (EPI_STORE only)
+    uint32_t o[8];
+    if (g.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(g.bias + col);
+      uint32_t bu[8];
+      *reinterpret_cast<uint4*>(&bu[0]) = __ldg(bp);
+      *reinterpret_cast<uint4*>(&bu[4]) = __ldg(bp + 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 b = unpack_bf162(bu[i]);
+        o[i] = pack_bf162(round_bf16(__uint_as_float(r[2 * i])) + b.x, round_bf16(__uint_as_float(r[2 * i + 1])) + b.y);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = pack_bf162(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    }
+    uint4* op = reinterpret_cast<uint4*>(g.out + (long long)row * g.ldo + col);
+    op[0] = *reinterpret_cast<uint4*>(&o[0]);
+    op[1] = *reinterpret_cast<uint4*>(&o[4]);
+    return;
+  }
   float y[16];
   if constexpr (MODE == B_I8) {
     if (g.epi == EPI_I32) {
@@ -234,8 +256,12 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, int row, int col, 
 // exponent pattern 0x6400 makes each half the fp16 value 1024 + q exactly;
 // subtracting 1024 leaves the exact integer q; one fused multiply-add applies
 // the group scale and scaled zero (rounded once, as the reference's __hfma2).
-__device__ __forceinline__ void dequant_chunk(const uint32_t (&x)[4], __half2 s2, __half2 z2, uint4 (&out)[4]) {
-  const __half2 magic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+// BF = true: the bf16 form (dequantize.cuh:53-90) -- exponent pattern 0x4300
+// (bf16 128 + q, exact since the bf16 spacing at 128 is 1), subtract 128, one
+// bf16x2 fma.  s2 / z2 hold the scale and scaled zero in both halves.
+template <bool BF = false>
+__device__ __forceinline__ void dequant_chunk(const uint32_t (&x)[4], uint32_t s2, uint32_t z2, uint4 (&out)[4]) {
+  constexpr uint32_t kMagic = BF ? 0x43004300u : 0x64006400u;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t o[4];
@@ -243,13 +269,28 @@ __device__ __forceinline__ void dequant_chunk(const uint32_t (&x)[4], __half2 s2
     for (int u = 0; u < 4; ++u) {
       uint32_t t;
       const uint32_t src = x[u] >> (4 * q);
-      asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(0x64006400u));
-      __half2 hq = __hsub2(*reinterpret_cast<__half2*>(&t), magic);
-      __half2 w = __hfma2(hq, s2, z2);
-      o[u] = *reinterpret_cast<uint32_t*>(&w);
+      asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(kMagic));
+      if constexpr (BF) {
+        using T2 = __nv_bfloat162;
+        const uint32_t m = kMagic;
+        const T2 w = __hfma2(__hsub2(*reinterpret_cast<const T2*>(&t), *reinterpret_cast<const T2*>(&m)),
+                             *reinterpret_cast<const T2*>(&s2), *reinterpret_cast<const T2*>(&z2));
+        o[u] = *reinterpret_cast<const uint32_t*>(&w);
+      } else {
+        using T2 = __half2;
+        const uint32_t m = kMagic;
+        const T2 w = __hfma2(__hsub2(*reinterpret_cast<const T2*>(&t), *reinterpret_cast<const T2*>(&m)),
+                             *reinterpret_cast<const T2*>(&s2), *reinterpret_cast<const T2*>(&z2));
+        o[u] = *reinterpret_cast<const uint32_t*>(&w);
+      }
     }
     out[q] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+}
+// Both halves of a 32-bit word set to one 16-bit value (scale / scaled zero).
+__device__ __forceinline__ uint32_t dup16(const void* p) {
+  const uint32_t v = *reinterpret_cast<const uint16_t*>(p);
+  return v | (v << 16);
 }
 
 

@@ -32,19 +32,19 @@ constexpr int KB_BYTES = 128;  // bytes of K per k-block (64 fp16 or 128 int8)
 
 template <int BN, int MODE>
 struct Cfg {
-  static constexpr int NS = (MODE == B_W4) ? (BN == 256 ? 4 : 6) : (BN == 256 ? 4 : 6);
-  static constexpr int ND = (MODE == B_W4) ? 3 : 0;
+  static constexpr int NS = (mode_is_w4(MODE)) ? (BN == 256 ? 4 : 6) : (BN == 256 ? 4 : 6);
+  static constexpr int ND = (mode_is_w4(MODE)) ? 3 : 0;
   static constexpr int A_BYTES = BM * KB_BYTES;                           // 16 KB
   static constexpr int B_BYTES = BN * KB_BYTES;                           // fp16/int8 operand tile
-  static constexpr int BQ_BYTES = (MODE == B_W4) ? (BN / 4) * KB_BYTES : 0; // packed int4 tile
-  static constexpr int SZ_BYTES = (MODE == B_W4) ? 2 * BN * 2 : 0;         // scales + zeros
-  static constexpr int NUM_DQ_WARPS = (MODE == B_W4) ? BN / 32 : 0;
+  static constexpr int BQ_BYTES = (mode_is_w4(MODE)) ? (BN / 4) * KB_BYTES : 0; // packed int4 tile
+  static constexpr int SZ_BYTES = (mode_is_w4(MODE)) ? 2 * BN * 2 : 0;         // scales + zeros
+  static constexpr int NUM_DQ_WARPS = (mode_is_w4(MODE)) ? BN / 32 : 0;
   static constexpr int THREADS = 256 + NUM_DQ_WARPS * 32;
   // shared memory carve-up (offsets from a 1024-aligned base)
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + NS * A_BYTES;                      // B_F16/B_I8 operand stages
   static constexpr int OFF_BQ = OFF_A + NS * A_BYTES;                     // B_W4 packed stages
-  static constexpr int OFF_D = (MODE == B_W4) ? OFF_BQ + NS * BQ_BYTES : OFF_B + NS * B_BYTES;
+  static constexpr int OFF_D = (mode_is_w4(MODE)) ? OFF_BQ + NS * BQ_BYTES : OFF_B + NS * B_BYTES;
   static constexpr int OFF_SZ = OFF_D + ND * B_BYTES;
   static constexpr int OFF_BAR = ((OFF_SZ + NS * SZ_BYTES) + 15) / 16 * 16;
   static constexpr int NUM_BARS = 4 * NS + 2 * ND + 4 + 1;
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       tma_prefetch_desc(&tmS);
       tma_prefetch_desc(&tmZ);
     }
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
           const uint32_t ph = (it / C::NS) & 1;
           if (!mbar_wait(&empty_a[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
           uint8_t* sa = smem + C::OFF_A + s * C::A_BYTES;
-          if constexpr (MODE == B_W4) {
+          if constexpr (mode_is_w4(MODE)) {
             mbar_arrive_expect_tx(&full_a[s], C::A_BYTES);
             tma_load_2d(sa, &tmA, &full_a[s], kb * 64, m_blk * BM);
             if (!mbar_wait(&empty_b[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ++it; ok = false; break; }
@@ -154,14 +154,14 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
           const uint32_t cnt = issued > (uint32_t)s ? (issued - 1 - s) / C::NS + 1 : 0;
           if (cnt == 0) continue;
           mbar_wait_drain(&full_a[s], (cnt - 1) & 1, 200000000ull);
-          if constexpr (MODE == B_W4) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
+          if constexpr (mode_is_w4(MODE)) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = (MODE == B_I8) ? idesc_i8(BM, BN) : idesc_f16(BM, BN);
+      constexpr uint32_t idesc = (MODE == B_I8) ? idesc_i8(BM, BN) : idesc_f16(BM, BN, false, false, MODE == B_W4BF);
       uint32_t it = 0;
       int t_local = 0;
       bool ok = true;
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
           if (!mbar_wait(&full_a[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           const uint8_t* sb;
           int d = 0;
-          if constexpr (MODE == B_W4) {
+          if constexpr (mode_is_w4(MODE)) {
             d = it % C::ND;
             const uint32_t dph = (it / C::ND) & 1;
             if (!mbar_wait(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
               mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0);
           }
           tc_commit(&empty_a[s]);
-          if constexpr (MODE == B_W4) tc_commit(&empty_d[d]);
+          if constexpr (mode_is_w4(MODE)) tc_commit(&empty_d[d]);
         }
         if (!ok) break;
         tc_commit(&tmem_full[acc]);
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
       tc_fence_after();
       const int row = m_blk * BM + q * 32 + lane;
       const uint32_t tbase = tmem_addr(tmem_base, q * 32, acc * BN);
-      if (MODE != B_I8 && g.epi == EPI_QKV_ROPE) {
+      if (MODE != B_I8 && MODE != B_W4BF && g.epi == EPI_QKV_ROPE) {
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           uint32_t r[64];
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequantisation
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       const int n = threadIdx.x - 256;  // channel within the tile, 0..BN-1
       const int grow = n >> 2;          // packed row within the tile
       const int ci = n & 3;             // channel within the packed row
@@ -256,12 +256,12 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
           const uint32_t ph = (it / C::NS) & 1;
           if (!mbar_wait_warp(&full_b[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           const uint8_t* sq = smem + C::OFF_BQ + s * C::BQ_BYTES + grow * 128;
-          const __half* ssz = reinterpret_cast<const __half*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
+          const uint16_t* ssz = reinterpret_cast<const uint16_t*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
           uint32_t x0[4], x1[4];
           *reinterpret_cast<uint4*>(x0) = *reinterpret_cast<const uint4*>(sq + (((2 * ci) ^ (grow & 7)) * 16));
           *reinterpret_cast<uint4*>(x1) = *reinterpret_cast<const uint4*>(sq + (((2 * ci + 1) ^ (grow & 7)) * 16));
-          const __half2 s2 = __half2half2(ssz[n]);
-          const __half2 z2 = __half2half2(ssz[BN + n]);
+          const uint32_t s2 = dup16(ssz + n);
+          const uint32_t z2 = dup16(ssz + BN + n);
           // the stage is refilled by TMA once released: retire these reads first
           fence_proxy_async_smem();
           __syncwarp();
@@ -271,10 +271,10 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
           if (!mbar_wait_warp(&empty_d[d], dph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
           uint8_t* drow = smem + C::OFF_D + d * C::B_BYTES + n * 128;
           uint4 o[4];
-          dequant_chunk(x0, s2, z2, o);
+          dequant_chunk<MODE == B_W4BF>(x0, s2, z2, o);
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + ((qq ^ (n & 7)) * 16)) = o[qq];
-          dequant_chunk(x1, s2, z2, o);
+          dequant_chunk<MODE == B_W4BF>(x1, s2, z2, o);
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
           fence_proxy_async_smem();
@@ -303,6 +303,8 @@ int launch_gemm(const GemmLaunch& L) {
                      di.max_smem_optin);
   CUtensorMap tmA, tmB, tmS, tmZ;
   int rc;
+  constexpr CUtensorMapDataType act_type =
+      MODE == B_W4BF ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   if constexpr (MODE == B_I8) {
     rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.a, L.K, L.M, L.lda, 128, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -311,16 +313,16 @@ int launch_gemm(const GemmLaunch& L) {
     tmS = tmB;
     tmZ = tmB;
   } else {
-    rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.a, L.K, L.M, L.lda * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = tmap_2d(&tmA, act_type, L.a, L.K, L.M, L.lda * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT16, L.b, L.K, L.N / 4, L.K * 2, 64, BN / 4,
                    CU_TENSOR_MAP_SWIZZLE_128B);
       if (rc) return rc;
-      rc = tmap_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.scales, L.N, L.gpad, L.N * 2, BN, 1,
+      rc = tmap_2d(&tmS, act_type, L.scales, L.N, L.gpad, L.N * 2, BN, 1,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc) return rc;
-      rc = tmap_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.zeros, L.N, L.gpad, L.N * 2, BN, 1,
+      rc = tmap_2d(&tmZ, act_type, L.zeros, L.N, L.gpad, L.N * 2, BN, 1,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc) return rc;
     } else {
@@ -372,7 +374,10 @@ int gemm_launch(const GemmLaunch& L) {
     return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: K=%lld must be a multiple of %d", (long long)L.K, kmul);
   if (!aligned16(L.a) || !aligned16(L.b) || !aligned16(L.out) || (L.bias && !aligned16(L.bias)))
     return set_error(QVGGT_ERR_ALIGN, "gemm: operands must be 16-byte aligned");
-  if (L.mode == B_W4) {
+  if (L.mode < B_W4 || L.mode > B_W4BF) return set_error(QVGGT_ERR_INVALID, "gemm: mode %d", L.mode);
+  if (L.mode == B_W4BF && L.epi != EPI_STORE)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: bf16 activations take the plain store epilogue only");
+  if (mode_is_w4(L.mode)) {
     if (L.group_size <= 0 || L.group_size % 64 != 0 || L.K % L.group_size != 0)
       return set_error(QVGGT_ERR_UNSUPPORTED, "gemm: group_size=%d must be a multiple of 64 dividing K=%lld",
                        L.group_size, (long long)L.K);
@@ -403,12 +408,14 @@ int gemm_launch(const GemmLaunch& L) {
     case GEMM_CFG_1SM_256:
       switch (L.mode) {
         case B_W4: return launch_gemm<256, B_W4>(L);
+        case B_W4BF: return launch_gemm<256, B_W4BF>(L);
         case B_F16: return launch_gemm<256, B_F16>(L);
         default: return launch_gemm<256, B_I8>(L);
       }
     default:
       switch (L.mode) {
         case B_W4: return launch_gemm<128, B_W4>(L);
+        case B_W4BF: return launch_gemm<128, B_W4BF>(L);
         case B_F16: return launch_gemm<128, B_F16>(L);
         default: return launch_gemm<128, B_I8>(L);
       }
@@ -445,7 +452,7 @@ int choose_gemm_config(int mode, long long M, long long N, int sms, bool can_pai
                                     {1000.0, 760.0, 540.0},
                                     {1250.0, 1100.0, 780.0},
                                     {0.0, 1216.0, 850.0}};
-  const int m = mode < 0 || mode > 2 ? 1 : mode;
+  const int m = mode == B_W4BF ? B_W4 : (mode < 0 || mode > 2 ? 1 : mode);
   double best = 1e300;
   int pick = GEMM_CFG_1SM_128;
   auto consider = [&](int cfg, long long tiles, int slots, double tile_flop, double r) {

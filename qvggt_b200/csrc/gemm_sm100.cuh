@@ -6,7 +6,10 @@
 
 namespace qv {
 
-enum GemmMode { B_W4 = 0, B_F16 = 1, B_I8 = 2 };
+// B_W4BF: B_W4 with bf16 activations, scales, scaled zeros, bias and output
+// (the reference's bf16 instantiation of the same kernels); EPI_STORE only.
+enum GemmMode { B_W4 = 0, B_F16 = 1, B_I8 = 2, B_W4BF = 3 };
+__host__ __device__ constexpr bool mode_is_w4(int mode) { return mode == B_W4 || mode == B_W4BF; }
 enum GemmEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_I32 = 3, EPI_QKV_ROPE = 4 };
 
 // EPI_QKV_ROPE: the output columns are [q | k | v] (each `dim` wide, heads of

@@ -48,14 +48,14 @@ constexpr int HBN = PBN / 2;
 template <int MODE>
 struct Cfg2 {
   static constexpr int NS = 6;
-  static constexpr int ND = (MODE == B_W4) ? 4 : 0;
+  static constexpr int ND = (mode_is_w4(MODE)) ? 4 : 0;
   static constexpr int A_BYTES = HM * KBB;                                  // 16 KB
   static constexpr int B_BYTES = HBN * KBB;                                 // 16 KB: this CTA's half
-  static constexpr int BQ_BYTES = (MODE == B_W4) ? (HBN / 4) * KBB : 0;     // 4 KB packed int4
-  static constexpr int SZ_BYTES = (MODE == B_W4) ? 2 * HBN * 2 : 0;         // scales + zeros
+  static constexpr int BQ_BYTES = (mode_is_w4(MODE)) ? (HBN / 4) * KBB : 0;     // 4 KB packed int4
+  static constexpr int SZ_BYTES = (mode_is_w4(MODE)) ? 2 * HBN * 2 : 0;         // scales + zeros
   // W4: two groups of HBN/32 dequantisation warps take alternate k-blocks, so
   // two k-blocks are dequantised at once (NS and ND are even).
-  static constexpr int DQ_GROUP_WARPS = (MODE == B_W4) ? HBN / 32 : 0;
+  static constexpr int DQ_GROUP_WARPS = (mode_is_w4(MODE)) ? HBN / 32 : 0;
   static constexpr int NUM_DQ_WARPS = 2 * DQ_GROUP_WARPS;
   static constexpr int THREADS = 256 + NUM_DQ_WARPS * 32;
   static_assert(NS % 2 == 0 && (ND % 2 == 0), "dequant groups alternate stages");
@@ -68,11 +68,11 @@ struct Cfg2 {
   // done, read from empty[(j - ND) % NS].  NS - ND even and positive: the next
   // phase of that barrier needs the MMAs of j - ND + NS, whose B the same
   // dequant group produces after k-block j, so the parity wait cannot alias.
-  static_assert(MODE != B_W4 || (NS > ND && (NS - ND) % 2 == 0), "W4 buffer reuse needs NS - ND even, > 0");
+  static_assert(!mode_is_w4(MODE) || (NS > ND && (NS - ND) % 2 == 0), "W4 buffer reuse needs NS - ND even, > 0");
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_A = 1024;
   static constexpr int OFF_B = OFF_A + NS * A_BYTES;                        // dense B stages / W4 packed stages
-  static constexpr int OFF_D = OFF_B + NS * ((MODE == B_W4) ? BQ_BYTES : B_BYTES);
+  static constexpr int OFF_D = OFF_B + NS * ((mode_is_w4(MODE)) ? BQ_BYTES : B_BYTES);
   static constexpr int OFF_SZ = OFF_D + ND * B_BYTES;
   static constexpr int END = OFF_SZ + NS * SZ_BYTES;
   static constexpr int SMEM = END + HBN * KBB + 1024;                       // + guard + alignment slack
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       tma_prefetch_desc(&tmS);
       tma_prefetch_desc(&tmZ);
     }
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = g.num_kb;
 
-  if (warp == 0 || (MODE == B_W4 && warp == 2)) {
+  if (warp == 0 || (mode_is_w4(MODE) && warp == 2)) {
     // ------------------------------------------------------------ producers (both CTAs)
     // Warp 0 loads A (and, dense / int8, B) into the stage ring paced by the
     // MMAs (`empty`).  W4: warp 2 loads the packed weights, scales and zeros
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     // read them (`empty_b`), so the dequantisation of a k-block never waits
     // behind the A tile of an earlier one.
     if (lane == 0) {
-      const bool b_role = MODE == B_W4 && warp == 2;
+      const bool b_role = mode_is_w4(MODE) && warp == 2;
       uint32_t it = 0;
       bool ok = true;
       for (int tile = cluster; tile < g.num_tiles && ok; tile += num_clusters) {
@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           const uint32_t full_lead = mapa_shared(&full[s], 0);
           uint8_t* sa = smem + C::OFF_A + s * C::A_BYTES;
           const int kx = kb * KBB / (MODE == B_I8 ? 1 : 2);
-          if constexpr (MODE == B_W4) {
+          if constexpr (mode_is_w4(MODE)) {
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
             tma_load_2d_pair(sa, &tmA, full_lead, kx, row0);
           } else {
@@ -209,14 +209,14 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = (MODE == B_I8) ? idesc_i8(2 * HM, PBN) : idesc_f16(2 * HM, PBN);
+      constexpr uint32_t idesc = (MODE == B_I8) ? idesc_i8(2 * HM, PBN) : idesc_f16(2 * HM, PBN, false, false, MODE == B_W4BF);
       // This single thread paces the tensor core, so its per-k-block path is
       // kept short: stage / phase / dequant-buffer indices advance
       // incrementally, and the shared-memory descriptors are built once per
       // buffer base and advanced by adding the encoded byte offset (the start
       // address field holds address >> 4 and cannot carry below 256 KB).
       const uint64_t a_desc0 = sdesc_sw128(smem_u32(smem + C::OFF_A));
-      const uint64_t b_desc0 = sdesc_sw128(smem_u32(smem + ((MODE == B_W4) ? C::OFF_D : C::OFF_B)));
+      const uint64_t b_desc0 = sdesc_sw128(smem_u32(smem + ((mode_is_w4(MODE)) ? C::OFF_D : C::OFF_B)));
       int s = 0, d = 0;
       uint32_t ph = 0, dph = 0;
       int t_local = 0;
@@ -233,9 +233,9 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           // cluster-scope acquire costs ~0.2 us per k-block on B200.  In W4
           // mode the even CTA's dequant warps have waited on it before
           // signalling full_d.
-          if (MODE != B_W4 && !mbar_wait(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
+          if (!mode_is_w4(MODE) && !mbar_wait(&full[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           uint64_t bd;
-          if constexpr (MODE == B_W4) {
+          if constexpr (mode_is_w4(MODE)) {
             // completes through both CTAs' signal copies (complete_tx):
             // CTA scope, like `full`; then arm the buffer's next phase (its
             // copies come only after the commit below frees the buffer)
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
               mma_f16_ss_pair(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
           }
           tc_commit_pair(&empty[s], 3);
-          if constexpr (MODE == B_W4) {
+          if constexpr (mode_is_w4(MODE)) {
             if (++d == C::ND) { d = 0; dph ^= 1; }
           }
           if (++s == C::NS) { s = 0; ph ^= 1; }
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
       tc_fence_after();
       const int row = m_blk * 2 * HM + (int)rank * HM + q * 32 + lane;
       const uint32_t tbase = tmem_addr(tmem_base, q * 32, acc * PBN);
-      if (MODE != B_I8 && g.epi == EPI_QKV_ROPE) {
+      if (MODE != B_I8 && MODE != B_W4BF && g.epi == EPI_QKV_ROPE) {
 #pragma unroll 1
         for (int c = 0; c < PBN / 64; ++c) {
           uint32_t r[64];
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequantisation (both CTAs)
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       const int dq = threadIdx.x - 256;
       const uint32_t group = (uint32_t)(dq / HBN);   // takes the k-blocks with it % 2 == group
       const int n = dq % HBN;           // local output channel, 0..HBN-1
@@ -324,12 +324,12 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           const uint32_t ph = (it / C::NS) & 1;
           if (!mbar_wait_warp(&full_b[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
           const uint8_t* sq = smem + C::OFF_B + s * C::BQ_BYTES + grow * 128;
-          const __half* ssz = reinterpret_cast<const __half*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
+          const uint16_t* ssz = reinterpret_cast<const uint16_t*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
           uint32_t x0[4], x1[4];
           *reinterpret_cast<uint4*>(x0) = *reinterpret_cast<const uint4*>(sq + (((2 * ci) ^ (grow & 7)) * 16));
           *reinterpret_cast<uint4*>(x1) = *reinterpret_cast<const uint4*>(sq + (((2 * ci + 1) ^ (grow & 7)) * 16));
-          const __half2 s2 = __half2half2(ssz[n]);
-          const __half2 z2 = __half2half2(ssz[HBN + n]);
+          const uint32_t s2 = dup16(ssz + n);
+          const uint32_t z2 = dup16(ssz + HBN + n);
           // the stage is refilled by TMA once released: retire these reads first
           fence_proxy_async_smem();
           __syncwarp();
@@ -345,10 +345,10 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
           }
           uint8_t* drow = smem + C::OFF_D + d * C::B_BYTES + n * 128;
           uint4 o[4];
-          dequant_chunk(x0, s2, z2, o);
+          dequant_chunk<MODE == B_W4BF>(x0, s2, z2, o);
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + ((qq ^ (n & 7)) * 16)) = o[qq];
-          dequant_chunk(x1, s2, z2, o);
+          dequant_chunk<MODE == B_W4BF>(x1, s2, z2, o);
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
           fence_proxy_async_smem();
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
-  if constexpr (MODE == B_W4) {
+  if constexpr (mode_is_w4(MODE)) {
     // After an abort, W4 signal copies issued before the cluster barrier may
     // still be in flight: let them land before either CTA exits.
     if (*abort_flag) {
@@ -391,6 +391,8 @@ int launch2(const GemmLaunch& L) {
     return set_error(QVGGT_ERR_UNSUPPORTED, "gemm2sm: %d B shared memory exceeds %d", C::SMEM, di.max_smem_optin);
   CUtensorMap tmA, tmB, tmS, tmZ;
   int rc;
+  constexpr CUtensorMapDataType act_type =
+      MODE == B_W4BF ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   if constexpr (MODE == B_I8) {
     rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.a, L.K, L.M, L.lda, 128, HM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -399,16 +401,16 @@ int launch2(const GemmLaunch& L) {
     tmS = tmB;
     tmZ = tmB;
   } else {
-    rc = tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.a, L.K, L.M, L.lda * 2, 64, HM, CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = tmap_2d(&tmA, act_type, L.a, L.K, L.M, L.lda * 2, 64, HM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       rc = tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT16, L.b, L.K, L.N / 4, L.K * 2, 64, HBN / 4,
                    CU_TENSOR_MAP_SWIZZLE_128B);
       if (rc) return rc;
-      rc = tmap_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.scales, L.N, L.gpad, L.N * 2, HBN, 1,
+      rc = tmap_2d(&tmS, act_type, L.scales, L.N, L.gpad, L.N * 2, HBN, 1,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc) return rc;
-      rc = tmap_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.zeros, L.N, L.gpad, L.N * 2, HBN, 1,
+      rc = tmap_2d(&tmZ, act_type, L.zeros, L.N, L.gpad, L.N * 2, HBN, 1,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc) return rc;
     } else {
@@ -469,6 +471,7 @@ int launch2(const GemmLaunch& L) {
 int gemm_launch_2sm(const GemmLaunch& L) {
   switch (L.mode) {
     case B_W4: return launch2<B_W4>(L);
+    case B_W4BF: return launch2<B_W4BF>(L);
     case B_F16: return launch2<B_F16>(L);
     case B_I8: return launch2<B_I8>(L);
   }

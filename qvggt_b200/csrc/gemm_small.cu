@@ -33,16 +33,16 @@ constexpr int MAX_SPLITS = 8;    // portable cluster size
 template <int MT, int MODE>
 struct SCfg {
   static constexpr int NS = MT <= 32 ? 8 : (MT <= 128 ? 6 : 4);
-  static constexpr int ND = (MODE == B_W4) ? 2 : 0;
+  static constexpr int ND = (mode_is_w4(MODE)) ? 2 : 0;
   static constexpr int X_BYTES = MT * 128;                                 // MT rows x 64 fp16
   static constexpr int W_BYTES = SBN * 128;                                // fp16 weight tile
-  static constexpr int BQ_BYTES = (MODE == B_W4) ? (SBN / 4) * 128 : 0;     // packed int4 tile
-  static constexpr int SZ_BYTES = (MODE == B_W4) ? 2 * SBN * 2 : 0;         // scales + zeros
-  static constexpr int NUM_DQ_WARPS = (MODE == B_W4) ? SBN / 32 : 0;
+  static constexpr int BQ_BYTES = (mode_is_w4(MODE)) ? (SBN / 4) * 128 : 0;     // packed int4 tile
+  static constexpr int SZ_BYTES = (mode_is_w4(MODE)) ? 2 * SBN * 2 : 0;         // scales + zeros
+  static constexpr int NUM_DQ_WARPS = (mode_is_w4(MODE)) ? SBN / 32 : 0;
   static constexpr int THREADS = 256 + NUM_DQ_WARPS * 32;
   static constexpr int OFF_X = 0;
   static constexpr int OFF_W = OFF_X + NS * X_BYTES;                       // dense W stages or packed stages
-  static constexpr int OFF_D = OFF_W + NS * ((MODE == B_W4) ? BQ_BYTES : W_BYTES);
+  static constexpr int OFF_D = OFF_W + NS * ((mode_is_w4(MODE)) ? BQ_BYTES : W_BYTES);
   static constexpr int OFF_SZ = OFF_D + ND * W_BYTES;
   static constexpr int OFF_BAR = ((OFF_SZ + NS * SZ_BYTES) + 15) / 16 * 16;
   static constexpr int NUM_BARS = 4 * NS + 2 * ND + 2;
@@ -64,8 +64,11 @@ using namespace gemmk;
 
 // The W4A16 / fp16 epilogue of one element (same rounding points as the large
 // kernel's epilogue16): y = half(half(acc) + bias), then GELU or
-// resid + half(y * gamma).
+// resid + half(y * gamma).  B_W4BF: bf16(acc) + bias, rounded to bf16 by the
+// store.
+template <int MODE>
 __device__ __forceinline__ float small_final(const GemmArgs& g, float y, float b, int m, int n) {
+  if constexpr (MODE == B_W4BF) return g.bias != nullptr ? round_bf16(y) + b : y;
   y = round_f16(y);
   if (g.bias != nullptr) y = round_f16(y + b);
   if (g.epi == EPI_GELU) {
@@ -128,7 +131,7 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       tma_prefetch_desc(&tmS);
       tma_prefetch_desc(&tmZ);
     }
@@ -149,7 +152,7 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
         const uint32_t ph = (it / C::NS) & 1;
         if (!mbar_wait(&empty_a[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
         uint8_t* sx = smem + C::OFF_X + s * C::X_BYTES;
-        if constexpr (MODE == B_W4) {
+        if constexpr (mode_is_w4(MODE)) {
           mbar_arrive_expect_tx(&full_a[s], C::X_BYTES);
           tma_load_2d(sx, &tmX, &full_a[s], kb * 64, 0);
           if (!mbar_wait(&empty_b[s], ph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_TMA_EMPTY)) { ++it; ok = false; break; }
@@ -174,14 +177,14 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
           const int cnt = issued > s ? (issued - 1 - s) / C::NS + 1 : 0;
           if (cnt == 0) continue;
           mbar_wait_drain(&full_a[s], (cnt - 1) & 1, 200000000ull);
-          if constexpr (MODE == B_W4) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
+          if constexpr (mode_is_w4(MODE)) mbar_wait_drain(&full_b[s], (cnt - 1) & 1, 200000000ull);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(SBN, MT);
+      constexpr uint32_t idesc = idesc_f16(SBN, MT, false, false, MODE == B_W4BF);
       bool ok = true;
       for (int it = 0; it < nkb; ++it) {
         const int s = it % C::NS;
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
         if (!mbar_wait(&full_a[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) { ok = false; break; }
         const uint8_t* sw;
         int d = 0;
-        if constexpr (MODE == B_W4) {
+        if constexpr (mode_is_w4(MODE)) {
           d = it % C::ND;
           const uint32_t dph = (it / C::ND) & 1;
           if (!mbar_wait(&full_d[d], dph, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) { ok = false; break; }
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
         for (int k = 0; k < 4; ++k)
           mma_f16_ss(tmem_base, sdesc_sw128(w_addr + k * 32), sdesc_sw128(x_addr + k * 32), idesc, (it | k) != 0);
         tc_commit(&empty_a[s]);
-        if constexpr (MODE == B_W4) tc_commit(&empty_d[d]);
+        if constexpr (mode_is_w4(MODE)) tc_commit(&empty_d[d]);
       }
       if (ok) {
         tc_commit(tmem_full);
@@ -223,7 +226,10 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
     const int n = n_blk * SBN + nl;
     if (mbar_wait_warp(tmem_full, 0, abort_flag, g.ctl, ST_TIMEOUT_TMEM)) {
       tc_fence_after();
-      const float b = (sa.splits == 1 && g.bias != nullptr) ? __half2float(g.bias[n]) : 0.f;
+      float b = 0.f;
+      if (sa.splits == 1 && g.bias != nullptr)
+        b = MODE == B_W4BF ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g.bias)[n])
+                           : __half2float(g.bias[n]);
 #pragma unroll 1
       for (int c = 0; c < MT / 16 && c * 16 < g.M; ++c) {
         uint32_t r[16];
@@ -235,14 +241,17 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
           const float acc = __uint_as_float(r[j]);
           if (sa.splits > 1)
             red[m * SBN + nl] = acc;
+          else if (m < g.M && MODE == B_W4BF)
+            reinterpret_cast<__nv_bfloat16*>(g.out)[(long long)m * g.ldo + n] =
+                __float2bfloat16_rn(small_final<MODE>(g, acc, b, m, n));
           else if (m < g.M)
-            g.out[(long long)m * g.ldo + n] = __float2half_rn(small_final(g, acc, b, m, n));
+            g.out[(long long)m * g.ldo + n] = __float2half_rn(small_final<MODE>(g, acc, b, m, n));
         }
       }
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequantisation
-    if constexpr (MODE == B_W4) {
+    if constexpr (mode_is_w4(MODE)) {
       const int n = threadIdx.x - 256;  // channel within the tile
       const int grow = n >> 2;          // packed row within the tile
       const int ci = n & 3;             // channel within the packed row
@@ -251,12 +260,12 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
         const uint32_t ph = (it / C::NS) & 1;
         if (!mbar_wait_warp(&full_b[s], ph, abort_flag, g.ctl, ST_TIMEOUT_FULL)) break;
         const uint8_t* sq = smem + C::OFF_W + s * C::BQ_BYTES + grow * 128;
-        const __half* ssz = reinterpret_cast<const __half*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
+        const uint16_t* ssz = reinterpret_cast<const uint16_t*>(smem + C::OFF_SZ + s * C::SZ_BYTES);
         uint32_t x0[4], x1[4];
         *reinterpret_cast<uint4*>(x0) = *reinterpret_cast<const uint4*>(sq + (((2 * ci) ^ (grow & 7)) * 16));
         *reinterpret_cast<uint4*>(x1) = *reinterpret_cast<const uint4*>(sq + (((2 * ci + 1) ^ (grow & 7)) * 16));
-        const __half2 s2 = __half2half2(ssz[n]);
-        const __half2 z2 = __half2half2(ssz[SBN + n]);
+        const uint32_t s2 = dup16(ssz + n);
+        const uint32_t z2 = dup16(ssz + SBN + n);
         // the stage is refilled by TMA once released: retire these reads first
         fence_proxy_async_smem();
         __syncwarp();
@@ -266,10 +275,10 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
         if (!mbar_wait_warp(&empty_d[d], dph ^ 1, abort_flag, g.ctl, ST_TIMEOUT_DEQ)) break;
         uint8_t* drow = smem + C::OFF_D + d * C::W_BYTES + n * 128;
         uint4 o[4];
-        dequant_chunk(x0, s2, z2, o);
+        dequant_chunk<MODE == B_W4BF>(x0, s2, z2, o);
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + ((qq ^ (n & 7)) * 16)) = o[qq];
-        dequant_chunk(x1, s2, z2, o);
+        dequant_chunk<MODE == B_W4BF>(x1, s2, z2, o);
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) *reinterpret_cast<uint4*>(drow + (((4 + qq) ^ (n & 7)) * 16)) = o[qq];
         fence_proxy_async_smem();
@@ -312,14 +321,17 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
       float b[4] = {0.f, 0.f, 0.f, 0.f};
       if (g.bias != nullptr) {
         const uint2 bu = *reinterpret_cast<const uint2*>(g.bias + n);
-        const float2 b01 = unpack_half2(bu.x), b23 = unpack_half2(bu.y);
+        const float2 b01 = MODE == B_W4BF ? unpack_bf162(bu.x) : unpack_half2(bu.x);
+        const float2 b23 = MODE == B_W4BF ? unpack_bf162(bu.y) : unpack_half2(bu.y);
         b[0] = b01.x; b[1] = b01.y; b[2] = b23.x; b[3] = b23.y;
       }
-      const float y0 = small_final(g, acc.x, b[0], m, n);
-      const float y1 = small_final(g, acc.y, b[1], m, n + 1);
-      const float y2 = small_final(g, acc.z, b[2], m, n + 2);
-      const float y3 = small_final(g, acc.w, b[3], m, n + 3);
-      *reinterpret_cast<uint2*>(g.out + (long long)m * g.ldo + n) = make_uint2(pack_half2(y0, y1), pack_half2(y2, y3));
+      const float y0 = small_final<MODE>(g, acc.x, b[0], m, n);
+      const float y1 = small_final<MODE>(g, acc.y, b[1], m, n + 1);
+      const float y2 = small_final<MODE>(g, acc.z, b[2], m, n + 2);
+      const float y3 = small_final<MODE>(g, acc.w, b[3], m, n + 3);
+      *reinterpret_cast<uint2*>(g.out + (long long)m * g.ldo + n) =
+          MODE == B_W4BF ? make_uint2(pack_bf162(y0, y1), pack_bf162(y2, y3))
+                         : make_uint2(pack_half2(y0, y1), pack_half2(y2, y3));
     }
   }
   // No CTA may exit (releasing its shared memory) while a peer still reads it.
@@ -371,8 +383,9 @@ int active_clusters(int splits) {
   return c;
 }
 
+// B_W4BF plans as B_W4: the same shared memory, threads and tiles.
 int plan_active_clusters(int mt, int mode, int splits) {
-  const bool w4 = mode == B_W4;
+  const bool w4 = mode_is_w4(mode);
   switch (mt) {
     case 16: return w4 ? active_clusters<16, B_W4>(splits) : active_clusters<16, B_F16>(splits);
     case 32: return w4 ? active_clusters<32, B_W4>(splits) : active_clusters<32, B_F16>(splits);
@@ -383,7 +396,7 @@ int plan_active_clusters(int mt, int mode, int splits) {
 }
 
 int plan_smem(int mt, int mode) {
-  const bool w4 = mode == B_W4;
+  const bool w4 = mode_is_w4(mode);
   switch (mt) {
     case 16: return w4 ? SCfg<16, B_W4>::SMEM : SCfg<16, B_F16>::SMEM;
     case 32: return w4 ? SCfg<32, B_W4>::SMEM : SCfg<32, B_F16>::SMEM;
@@ -397,16 +410,18 @@ template <int MT, int MODE>
 int launch_small(const GemmLaunch& L, const SmallPlan& P) {
   using C = SCfg<MT, MODE>;
   CUtensorMap tmX, tmW, tmS, tmZ;
-  int rc = tmap_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.a, L.K, L.M, L.lda * 2, 64, MT, CU_TENSOR_MAP_SWIZZLE_128B);
+  constexpr CUtensorMapDataType act_type =
+      MODE == B_W4BF ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int rc = tmap_2d(&tmX, act_type, L.a, L.K, L.M, L.lda * 2, 64, MT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if constexpr (MODE == B_W4) {
+  if constexpr (mode_is_w4(MODE)) {
     rc = tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT16, L.b, L.K, L.N / 4, L.K * 2, 64, SBN / 4,
                  CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    rc = tmap_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.scales, L.N, L.gpad, L.N * 2, SBN, 1,
+    rc = tmap_2d(&tmS, act_type, L.scales, L.N, L.gpad, L.N * 2, SBN, 1,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    rc = tmap_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.zeros, L.N, L.gpad, L.N * 2, SBN, 1,
+    rc = tmap_2d(&tmZ, act_type, L.zeros, L.N, L.gpad, L.N * 2, SBN, 1,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   } else {
@@ -458,7 +473,8 @@ int launch_small(const GemmLaunch& L, const SmallPlan& P) {
 }  // namespace
 
 int gemm_small_plan(int mode, long long M, long long N, long long K, int max_splits, SmallPlan* P) {
-  if (mode != B_W4 && mode != B_F16) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: mode %d", mode);
+  if (mode != B_W4 && mode != B_F16 && mode != B_W4BF)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: mode %d", mode);
   if (M < 1 || M > 256) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: M=%lld must be in 1..256", M);
   if (N <= 0 || N % SBN) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: N=%lld must be a multiple of 128", N);
   if (K <= 0 || K % 64) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: K=%lld must be a multiple of 64", K);
@@ -500,14 +516,16 @@ int gemm_small_plan(int mode, long long M, long long N, long long K, int max_spl
 }
 
 int gemm_small_launch(const GemmLaunch& L, const SmallPlan& P) {
-  if (L.mode != B_W4 && L.mode != B_F16) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: mode");
+  if (L.mode != B_W4 && L.mode != B_F16 && L.mode != B_W4BF) return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: mode");
   if (L.epi != EPI_STORE && L.epi != EPI_GELU && L.epi != EPI_RESID)
     return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: epilogue %d", L.epi);
+  if (L.mode == B_W4BF && L.epi != EPI_STORE)
+    return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: bf16 activations take the plain store epilogue only");
   if (!aligned16(L.a) || !aligned16(L.b) || !aligned16(L.out) || (L.bias && !aligned16(L.bias)))
     return set_error(QVGGT_ERR_ALIGN, "gemm_small: operands must be 16-byte aligned");
   if (L.lda % 8 || L.ldo % 8 || (L.resid && L.ldr % 8))
     return set_error(QVGGT_ERR_ALIGN, "gemm_small: strides must be multiples of 8 elements");
-  if (L.mode == B_W4) {
+  if (mode_is_w4(L.mode)) {
     if (L.group_size <= 0 || L.group_size % 64 != 0 || L.K % L.group_size != 0)
       return set_error(QVGGT_ERR_UNSUPPORTED, "gemm_small: group_size=%d must be a multiple of 64 dividing K",
                        L.group_size);
@@ -516,6 +534,16 @@ int gemm_small_launch(const GemmLaunch& L, const SmallPlan& P) {
   }
   if (L.epi == EPI_RESID && (!L.resid || !L.gamma)) return set_error(QVGGT_ERR_INVALID, "gemm_small: residual needs resid+gamma");
   if (P.splits < 1 || P.splits > MAX_SPLITS) return set_error(QVGGT_ERR_INVALID, "gemm_small: bad plan");
+  if (L.mode == B_W4BF) {
+    switch (P.mt) {
+      case 16: return launch_small<16, B_W4BF>(L, P);
+      case 32: return launch_small<32, B_W4BF>(L, P);
+      case 64: return launch_small<64, B_W4BF>(L, P);
+      case 128: return launch_small<128, B_W4BF>(L, P);
+      case 256: return launch_small<256, B_W4BF>(L, P);
+    }
+    return set_error(QVGGT_ERR_INVALID, "gemm_small: bad plan");
+  }
   const bool w4 = L.mode == B_W4;
   switch (P.mt) {
     case 16: return w4 ? launch_small<16, B_W4>(L, P) : launch_small<16, B_F16>(L, P);

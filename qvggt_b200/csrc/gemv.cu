@@ -14,7 +14,11 @@
 // reference's __hfma2); x . w is formed over each run of 8 consecutive k with
 // fp16x2 FMAs and that partial is added into an fp32 accumulator (the
 // reference's GEMV accumulates every product of a thread in fp16; a product
-// is exact when x is one-hot).
+// is exact when x is one-hot).  The bf16 form (BF) dequantises with the bf16
+// magic pattern and bf16x2 FMA (dequantize.cuh:53-90) and forms x . w in fp32
+// (bf16 widens to fp32 exactly; the reference accumulates in bf16).
+#include <type_traits>
+
 #include "host.hpp"
 
 namespace qv {
@@ -29,12 +33,20 @@ __device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
 }
 
-template <int MT, bool XS>
+template <int MT, bool XS, bool BF>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kernel(
-    const __half* __restrict__ x, const uint16_t* __restrict__ qw, const __half* __restrict__ scales,
-    const __half* __restrict__ zeros, const __half* __restrict__ bias, __half* __restrict__ out, int m, int N, int K,
+    const void* __restrict__ x_, const uint16_t* __restrict__ qw, const void* __restrict__ scales_,
+    const void* __restrict__ zeros_, const void* __restrict__ bias_, void* __restrict__ out_, int m, int N, int K,
     int G) {
-  extern __shared__ __align__(16) __half x_smem[];   // XS: x [m, K]
+  using T = std::conditional_t<BF, __nv_bfloat16, __half>;
+  using T2 = std::conditional_t<BF, __nv_bfloat162, __half2>;
+  const T* x = static_cast<const T*>(x_);
+  const T* scales = static_cast<const T*>(scales_);
+  const T* zeros = static_cast<const T*>(zeros_);
+  const T* bias = static_cast<const T*>(bias_);
+  T* out = static_cast<T*>(out_);
+  extern __shared__ __align__(16) uint8_t x_smem_raw[];   // XS: x [m, K]
+  T* x_smem = reinterpret_cast<T*>(x_smem_raw);
   __shared__ float red[GEMV_ROWS][4][4][MT];          // [row][quarter][channel][m]
   if constexpr (XS) {
     const int chunks = m * K / 8;
@@ -51,13 +63,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kern
   // a 128-byte k-chunk c that is channel ci = (lane%8)/2, half h = lane%2.
   const int ci = (lane & 7) >> 1;
   const int h = lane & 1;
-  const __half2 magic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const uint32_t magic_u = BF ? 0x43004300u : 0x64006400u;
+  const T2 magic = *reinterpret_cast<const T2*>(&magic_u);
   float acc[MT];
 #pragma unroll
   for (int r = 0; r < MT; ++r) acc[r] = 0.f;
   for (int base = 0; base < row_bytes; base += GEMV_BATCH * 2048) {
     uint4 wvs[GEMV_BATCH];
-    __half ss[GEMV_BATCH], zs[GEMV_BATCH];
+    T ss[GEMV_BATCH], zs[GEMV_BATCH];
 #pragma unroll
     for (int it = 0; it < GEMV_BATCH; ++it) {
       const int off = base + ((it * 4 + wq) * 32 + lane) * 16;
@@ -79,18 +92,18 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kern
       if (off >= row_bytes) break;
       const int k0 = 64 * (off >> 7) + 32 * h;
       const uint4 wv = wvs[it];
-      const __half2 s2 = __half2half2(ss[it]), z2 = __half2half2(zs[it]);
+      const T2 s2 = T2(ss[it], ss[it]), z2 = T2(zs[it], zs[it]);
       const uint32_t xw[4] = {wv.x, wv.y, wv.z, wv.w};
-      // w[q][u] (dequantised fp16 pair) covers k = k0 + 8q + 2u, +1
-      __half2 w[4][4];
+      // w[q][u] (dequantised pair) covers k = k0 + 8q + 2u, +1
+      T2 w[4][4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint32_t t;
           const uint32_t src = xw[u] >> (4 * q);
-          asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(0x64006400u));
-          __half2 hq = __hsub2(*reinterpret_cast<__half2*>(&t), magic);
+          asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(magic_u));
+          const T2 hq = __hsub2(*reinterpret_cast<T2*>(&t), magic);
           w[q][u] = __hfma2(hq, s2, z2);
         }
       }
@@ -103,12 +116,22 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kern
           for (int q = 0; q < 4; ++q) {
             uint4 xv = XS ? xp[q] : __ldg(xp + q);
             const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
-            // x . w over these 8 k in fp16x2, then one fp32 add per half
-            __half2 p = __hmul2(*reinterpret_cast<const __half2*>(&xu[0]), w[q][0]);
+            if constexpr (BF) {
 #pragma unroll
-            for (int u = 1; u < 4; ++u) p = __hfma2(*reinterpret_cast<const __half2*>(&xu[u]), w[q][u], p);
-            const float2 pf = __half22float2(p);
-            a += pf.x + pf.y;
+              for (int u = 0; u < 4; ++u) {
+                const float2 xf = unpack_bf162(xu[u]);
+                const float2 wf = unpack_bf162(*reinterpret_cast<const uint32_t*>(&w[q][u]));
+                a = fmaf(xf.x, wf.x, a);
+                a = fmaf(xf.y, wf.y, a);
+              }
+            } else {
+              // x . w over these 8 k in fp16x2, then one fp32 add per half
+              __half2 p = __hmul2(*reinterpret_cast<const __half2*>(&xu[0]), w[q][0]);
+#pragma unroll
+              for (int u = 1; u < 4; ++u) p = __hfma2(*reinterpret_cast<const __half2*>(&xu[u]), w[q][u], p);
+              const float2 pf = __half22float2(p);
+              a += pf.x + pf.y;
+            }
           }
           acc[r] = a;
         }
@@ -136,9 +159,15 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kern
     if (gg >= N / 4 || r >= MT) continue;
     const float v = red[rr][0][ch][r] + red[rr][1][ch][r] + red[rr][2][ch][r] + red[rr][3][ch][r];
     const int n = 4 * gg + ch;
-    float y = round_f16(v);
-    if (bias) y = y + __half2float(bias[n]);
-    out[(size_t)r * N + n] = __float2half_rn(y);
+    if constexpr (BF) {
+      float y = round_bf16(v);
+      if (bias) y = y + __bfloat162float(bias[n]);
+      out[(size_t)r * N + n] = __float2bfloat16_rn(y);
+    } else {
+      float y = round_f16(v);
+      if (bias) y = y + __half2float(bias[n]);
+      out[(size_t)r * N + n] = __float2half_rn(y);
+    }
   }
 }
 
@@ -147,9 +176,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kern
 
 using namespace qv;
 
-extern "C" int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const void* scales,
-                                const void* scaled_zeros, const void* bias, void* out, int64_t m, int64_t N,
-                                int64_t K, int64_t gpad, int32_t group_size, void* stream) {
+namespace {
+
+int gemv_launch(bool bf16, const void* in_feats, const void* qweight, const void* scales, const void* scaled_zeros,
+                const void* bias, void* out, int64_t m, int64_t N, int64_t K, int64_t gpad, int32_t group_size,
+                void* stream) {
   if (m < 1 || m > 16) return set_error(QVGGT_ERR_UNSUPPORTED, "gemv: m=%lld must be in 1..16", (long long)m);
   if (N <= 0 || N % 4 || K <= 0 || K % 64)
     return set_error(QVGGT_ERR_INVALID, "gemv: N=%lld must be a multiple of 4, K=%lld of 64", (long long)N,
@@ -165,17 +196,18 @@ extern "C" int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const
   const int xs_bytes = (int)(m * K * 2);
   const bool xs = xs_bytes <= GEMV_XS_MAX;
   auto args = [&](auto kfn) {
-    kfn<<<grid, block, xs ? xs_bytes : 0, st>>>(static_cast<const __half*>(in_feats),
-                                                 static_cast<const uint16_t*>(qweight),
-                                                 static_cast<const __half*>(scales),
-                                                 static_cast<const __half*>(scaled_zeros),
-                                                 static_cast<const __half*>(bias), static_cast<__half*>(out), (int)m,
-                                                 (int)N, (int)K, group_size);
+    kfn<<<grid, block, xs ? xs_bytes : 0, st>>>(in_feats, static_cast<const uint16_t*>(qweight), scales,
+                                                 scaled_zeros, bias, out, (int)m, (int)N, (int)K, group_size);
   };
   auto by_m = [&](auto mt) {
     constexpr int MT = decltype(mt)::value;
-    if (xs) args(gemv_w4_kernel<MT, true>);
-    else args(gemv_w4_kernel<MT, false>);
+    if (bf16) {
+      if (xs) args(gemv_w4_kernel<MT, true, true>);
+      else args(gemv_w4_kernel<MT, false, true>);
+    } else {
+      if (xs) args(gemv_w4_kernel<MT, true, false>);
+      else args(gemv_w4_kernel<MT, false, false>);
+    }
   };
   if (K > 16384) return set_error(QVGGT_ERR_UNSUPPORTED, "gemv: K=%lld > 16384", (long long)K);
   if (m <= 1) by_m(std::integral_constant<int, 1>());
@@ -186,4 +218,18 @@ extern "C" int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const
   int rc = check_cuda(cudaGetLastError(), "gemv launch");
   if (rc == QVGGT_OK) count_launch(1);
   return rc;
+}
+
+}  // namespace
+
+extern "C" int qvggt_w4a16_gemv(const void* in_feats, const void* qweight, const void* scales,
+                                const void* scaled_zeros, const void* bias, void* out, int64_t m, int64_t N,
+                                int64_t K, int64_t gpad, int32_t group_size, void* stream) {
+  return gemv_launch(false, in_feats, qweight, scales, scaled_zeros, bias, out, m, N, K, gpad, group_size, stream);
+}
+
+extern "C" int qvggt_w4a16_gemv_bf16(const void* in_feats, const void* qweight, const void* scales,
+                                     const void* scaled_zeros, const void* bias, void* out, int64_t m, int64_t N,
+                                     int64_t K, int64_t gpad, int32_t group_size, void* stream) {
+  return gemv_launch(true, in_feats, qweight, scales, scaled_zeros, bias, out, m, N, K, gpad, group_size, stream);
 }

@@ -3,6 +3,7 @@
     python oracle/build_ref.py            # in the container with the reference checkout
     python tests/golden/make_ref_cuda_golden.py --out ref_cuda_golden.npz [--time]
     python tests/golden/make_ref_cuda_golden.py --gemm-pins ref_cuda_gemm_pins.npz
+    python tests/golden/make_ref_cuda_golden.py --bf16-pins ref_cuda_bf16_pins.npz
 
 Runs the reference kernels (built from their own sources into oracle/_ref/ by
 oracle/build_ref.py) on inputs generated from fixed seeds (regenerated
@@ -92,6 +93,62 @@ def gemm_pin_cases():
     x = np.random.default_rng(0).standard_normal((1374, 1024)).astype(np.float16)
     c["c0"] = dict(x=x, qweight=lin["qweight"], scales=lin["scales"], scaled_zeros=lin["scaled_zeros"])
     return c
+
+
+def bf16_pin_cases():
+    """Inputs of the bf16 pins: the reference's bf16 instantiation of
+    gemm_forward_cuda_new / gemv_forward_cuda_new (``dispatch_utils.cuh:7-17``).
+    bf16 tensors are held as float32 arrays of bf16 values (numpy has no bf16).
+
+    ``eye``: as :func:`gemm_pin_cases`' eye case in bf16 (A = I, M = K = 1024,
+    N = 512, scales over 2^-6 .. 2^6 times the config-0 distribution, all 16
+    nibble values and zero points): C = deq_bf16(W)^T bit for bit (one exact
+    product per output, fp32 accumulation, an exact bf16 store).
+    ``lin``: N = 512, K = 1024, g128 bf16 weights; X [300, 1024] ~ N(0, 1) in
+    bf16 for the GEMM (``gemm_w4a16_T2``), its first 1 and 5 rows for the GEMV.
+    """
+    from oracle import awq
+    c = {}
+    N, K, G = 512, 1024, 128
+    rng = np.random.default_rng(13)
+    q = rng.integers(0, 16, size=(N, K), dtype=np.int32)
+    zeros = rng.integers(0, 16, size=(N, K // G)).astype(np.float64)
+    mult = 2.0 ** rng.integers(-6, 7, size=(N, K // G))
+    scales = awq.bf16_round(np.maximum(np.abs(rng.standard_normal((N, K // G))) * 0.02 * mult, 1e-4))
+    gpad = awq.calculate_zeros_width(K, G) * 8
+    st = np.zeros((gpad, N), np.float32)
+    st[: K // G] = scales.T
+    szt = np.zeros((gpad, N), np.float32)
+    szt[: K // G] = awq.bf16_round(-(scales.astype(np.float64) * zeros)).T
+    c["eye"] = dict(x=np.eye(K, dtype=np.float32), qweight=awq.pack_intweight(q), scales=st, scaled_zeros=szt)
+    lin = awq.make_quantized_linear_bf16(N, K, G, seed=14, bias=False)
+    x = awq.bf16_round(np.random.default_rng(15).standard_normal((300, K)))
+    c["lin"] = dict(x=x, qweight=lin["qweight"], scales=lin["scales"], scaled_zeros=lin["scaled_zeros"])
+    return c
+
+
+def generate_bf16_pins(ref, dev="cuda"):
+    """Outputs (uint16 bf16 bit patterns) of the reference kernels on
+    :func:`bf16_pin_cases`."""
+    from oracle import awq
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16).to(dev)
+    qw = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    bits = lambda y: awq.bf16_bits(y.float().cpu().numpy())
+    c = bf16_pin_cases()
+    out = {}
+    d = c["eye"]
+    out["eye_y"] = bits(ref.gemm_forward_cuda_new(bf(d["x"]), qw(d["qweight"]), bf(d["scales"]),
+                                                  bf(d["scaled_zeros"])))
+    d = c["lin"]
+    out["gemm_y"] = bits(ref.gemm_forward_cuda_new(bf(d["x"]), qw(d["qweight"]), bf(d["scales"]),
+                                                   bf(d["scaled_zeros"])))
+    K, N = d["x"].shape[1], d["qweight"].shape[0] * 4
+    for m in (1, 5):
+        y = ref.gemv_forward_cuda_new(bf(d["x"][:m]), qw(d["qweight"]), bf(d["scales"]), bf(d["scaled_zeros"]), m, N,
+                                      K, 128)
+        out[f"gemv_m{m}_y"] = bits(y)
+    torch.cuda.synchronize()
+    return out
 
 
 def generate_gemm_pins(ref, dev="cuda"):
@@ -203,9 +260,15 @@ def main():
     ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "ref_cuda_golden.npz"))
     ap.add_argument("--time", action="store_true")
     ap.add_argument("--gemm-pins", default=None, help="write only the GEMM pin fixture to this path")
+    ap.add_argument("--bf16-pins", default=None, help="write only the bf16 GEMM / GEMV pin fixture to this path")
     a = ap.parse_args()
     from oracle import build_ref
     ref = build_ref.load()
+    if a.bf16_pins:
+        out = generate_bf16_pins(ref)
+        np.savez_compressed(a.bf16_pins, **out)
+        print("wrote", a.bf16_pins, {k: v.shape for k, v in out.items()})
+        return
     if a.gemm_pins:
         out = generate_gemm_pins(ref)
         np.savez_compressed(a.gemm_pins, **out)

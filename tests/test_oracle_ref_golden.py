@@ -115,3 +115,42 @@ def test_oracle_dequant_equals_reference_kernel_bit_for_bit():
     d = gemm_pin_cases()["eye"]
     deq = awq.dequantize(d["qweight"], d["scales"], d["scaled_zeros"], 128)      # [N, K] fp16
     assert np.array_equal(np.ascontiguousarray(deq.T).view(np.uint16), gold["eye_y"].view(np.uint16))
+
+
+BF16_PINS = os.path.join(HERE, "golden", "ref_cuda_bf16_pins.npz")
+
+
+@pytest.mark.skipif(not os.path.exists(BF16_PINS), reason="bf16 reference pins not generated")
+def test_oracle_bf16_dequant_equals_reference_kernel_bit_for_bit():
+    """The reference's bf16 ``gemm_forward_cuda_new`` with A = I returns its
+    bf16 dequantised weights; ``oracle.awq.dequantize_bf16`` (the bf16 unpack
+    and one bf16x2 fma, ``dequantize.cuh:53-90``) must equal them bit for bit."""
+    from tests.golden.make_ref_cuda_golden import bf16_pin_cases
+    d = bf16_pin_cases()["eye"]
+    deq = awq.dequantize_bf16(d["qweight"], d["scales"], d["scaled_zeros"], 128)      # [N, K]
+    assert np.array_equal(awq.bf16_bits(np.ascontiguousarray(deq.T)), np.load(BF16_PINS)["eye_y"])
+
+
+@pytest.mark.skipif(not os.path.exists(BF16_PINS), reason="bf16 reference pins not generated")
+def test_oracle_bf16_linear_near_reference_kernels():
+    """The float64 oracle against the reference's bf16 GEMM (fp32 accumulation:
+    max-abs-rel <= 8e-3) and GEMV (bf16 accumulation: rel-L2 <= 2e-2)."""
+    from tests.golden.make_ref_cuda_golden import bf16_pin_cases
+    d = bf16_pin_cases()["lin"]
+    pins = np.load(BF16_PINS)
+    ref = awq.w4a16_linear_bf16(d["x"], d["qweight"], d["scales"], d["scaled_zeros"], 128)
+    y = awq.from_bf16_bits(pins["gemm_y"])
+    assert awq.max_abs_rel(torch.from_numpy(y), torch.from_numpy(ref)) <= 8e-3
+    for m in (1, 5):
+        y = awq.from_bf16_bits(pins[f"gemv_m{m}_y"])
+        assert awq.rel_l2(torch.from_numpy(y), torch.from_numpy(ref[:m])) <= 2e-2
+
+
+def test_oracle_bf16_round_matches_torch():
+    """oracle.awq.bf16_round (one rounding from float64) equals torch's
+    float32 -> bf16 conversion on float32 inputs, ties included."""
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(20000) * 10.0 ** rng.integers(-6, 6, 20000)).astype(np.float32)
+    x[:4] = [1 + 2 ** -8, 1 + 3 * 2 ** -8, -(1 + 2 ** -8), 0.0]
+    want = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    assert np.array_equal(awq.bf16_round(x.astype(np.float64)), want)
