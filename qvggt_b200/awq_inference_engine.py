@@ -34,7 +34,14 @@ def _ptr(t):
     return None if t is None else C.c_void_p(t.data_ptr())
 
 
+# The current stream's raw handle without building a torch.cuda.Stream object
+# per call (the aggregator issues ~500 launches per forward).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: torch.Tensor):
+    if _raw_stream is not None:
+        return C.c_void_p(_raw_stream(t.device.index))
     return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
 
@@ -108,14 +115,23 @@ def _check_rows(name, t, rows: int, cols: int, what: str):
 
 
 class _Dev:
+    """Makes `dev` the current CUDA device for the launch (the C ABI launches
+    on the current device), restoring the previous one after; a no-op when
+    it already is current."""
+
     def __init__(self, dev):
-        self.g = torch.cuda.device(dev)
+        self.idx = dev.index
+        self.prev = None
 
     def __enter__(self):
-        self.g.__enter__()
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
 
     def __exit__(self, *a):
-        self.g.__exit__(*a)
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
 
 
 # --------------------------------------------------------------------- W4A16

@@ -374,6 +374,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // the prologue above touches no global memory: wait for the previous
+  // kernel in the stream only now (programmatic dependent launch)
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   const uint32_t misc = smem_u32(smem + AttnSmem::MISC);
 
@@ -880,8 +884,8 @@ int attention_launch(const void* q, int64_t q_stride, const void* kv, int64_t kv
                             "attention: clearing the split counters"))
       return rc;
   }
-  kfn<<<(unsigned)grid, THREADS, AttnSmem::TOTAL, st>>>(tmQ, tmK, tmV, a);
-  int rc = check_cuda(cudaGetLastError(), "attention launch");
+  int rc = check_cuda(launch_pdl(kfn, dim3((unsigned)grid), dim3(THREADS), AttnSmem::TOTAL, st, 1u, tmQ, tmK, tmV, a),
+                      "attention launch");
   if (!rc) count_launch(1);
   return rc;
 }

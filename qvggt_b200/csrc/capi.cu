@@ -2,6 +2,7 @@
 // encoding) and the GEMM entry points.  The other kernels' entry points live
 // beside their kernels.
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -52,6 +53,14 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("QVGGT_PDL");
+    return !(e && e[0] == '0' && e[1] == 0);
+  }();
+  return on;
+}
 
 const DeviceInfo& device_info() {
   const int dev = current_device();

@@ -29,6 +29,19 @@ struct Ctl {
   unsigned long long timeout_ns;
 };
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialisation attribute (launch_pdl) may be scheduled while the
+// kernel before it in the stream is still running: it runs its prologue
+// (barrier init, TMEM allocation, tensor-map prefetch), then pdl_wait() blocks
+// until that kernel has completed and its memory is visible.  No global
+// memory is read or written before pdl_wait().  pdl_trigger() lets the next
+// such kernel be scheduled once every CTA of this grid has started; it waits
+// in its own pdl_wait() for this grid to complete.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -112,6 +112,10 @@ __global__ void __launch_bounds__(Cfg<BN, MODE>::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // no global memory touched so far: wait for the previous kernel in the
+  // stream only now (programmatic dependent launch)
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_kb = g.num_kb;
@@ -358,8 +362,8 @@ int launch_gemm(const GemmLaunch& L) {
   static DeviceFlags attr_set;
   if ((rc = ensure_smem(attr_set, kfn, C::SMEM, "cudaFuncSetAttribute(gemm)"))) return rc;
   const int grid = g.num_tiles < di.num_sms ? g.num_tiles : di.num_sms;
-  kfn<<<grid, C::THREADS, C::SMEM, L.stream>>>(tmA, tmB, tmS, tmZ, g);
-  return check_cuda(cudaGetLastError(), "gemm launch");
+  return check_cuda(launch_pdl(kfn, dim3(grid), dim3(C::THREADS), C::SMEM, L.stream, 1u, tmA, tmB, tmS, tmZ, g),
+                    "gemm launch");
 }
 
 }  // namespace

@@ -145,6 +145,10 @@ __global__ void __launch_bounds__(Cfg2<MODE>::THREADS, 1)
   __syncthreads();
   cluster_sync();   // both CTAs' barriers exist before any cross-CTA signal
   tc_fence_after();
+  // no global memory touched so far: wait for the previous kernel in the
+  // stream only now (programmatic dependent launch)
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = g.num_kb;
 
@@ -447,19 +451,8 @@ int launch2(const GemmLaunch& L) {
   if ((rc = ensure_smem(attr_set, kfn, C::SMEM, "cudaFuncSetAttribute(gemm2sm)"))) return rc;
   const int max_clusters = di.num_sms / 2;
   const int clusters = g.num_tiles < max_clusters ? g.num_tiles : max_clusters;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(C::THREADS);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = L.stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  rc = check_cuda(cudaLaunchKernelEx(&cfg, kfn, tmA, tmB, tmS, tmZ, g), "gemm2sm launch");
+  rc = check_cuda(launch_pdl(kfn, dim3(2 * clusters), dim3(C::THREADS), C::SMEM, L.stream, 2u, tmA, tmB, tmS, tmZ, g),
+                  "gemm2sm launch");
   if (rc) return rc;
   return check_cuda(cudaGetLastError(), "gemm2sm launch");
 }

@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32) layernorm_kernel(const __
                                                                         const __half* __restrict__ w,
                                                                         const __half* __restrict__ b,
                                                                         __half* __restrict__ y, long long T, float eps) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int H = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROWS_PER_BLOCK + (threadIdx.x >> 5);
@@ -284,10 +286,12 @@ int qvggt_layernorm(const void* in, const void* gamma, const void* beta, void* o
   if (!gamma || !beta) return set_error(QVGGT_ERR_INVALID, "layernorm: gamma and beta required");
   if (tokens == 0) return QVGGT_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  QV_DISPATCH_CH_SMALL(hidden, layernorm_kernel<CH><<<rows_grid(tokens), ROWS_PER_BLOCK * 32, 0, st>>>(
-                             static_cast<const __half*>(in), static_cast<const __half*>(gamma),
-                             static_cast<const __half*>(beta), static_cast<__half*>(out), tokens, eps));
-  rc = check_cuda(cudaGetLastError(), "layernorm launch");
+  cudaError_t err = cudaSuccess;
+  QV_DISPATCH_CH_SMALL(hidden, err = launch_pdl(layernorm_kernel<CH>, dim3(rows_grid(tokens)), dim3(ROWS_PER_BLOCK * 32),
+                                                0, st, 1u, static_cast<const __half*>(in),
+                                                static_cast<const __half*>(gamma), static_cast<const __half*>(beta),
+                                                static_cast<__half*>(out), (long long)tokens, eps));
+  rc = check_cuda(err, "layernorm launch");
   if (!rc) count_launch(1);
   return rc;
 }

@@ -15,6 +15,8 @@ namespace {
 
 __global__ void patchify_kernel(const __half* __restrict__ img, __half* __restrict__ out, int S, int H, int W, int p,
                                 int kpad, float m0, float m1, float m2, float s0, float s1, float s2) {
+  pdl_wait();
+  pdl_trigger();
   const int gw = W / p, gh = H / p;
   const long long row = blockIdx.x;   // patch index over S * gh * gw
   const int f = (int)(row / (gh * gw));
@@ -39,6 +41,8 @@ __global__ void assemble_kernel(const __half* __restrict__ src, long long src_ro
                                 const __half* __restrict__ specials, int n_special, int two_sets,
                                 const __half* __restrict__ pos, __half* __restrict__ out, int P, int C,
                                 long long frame_offset) {
+  pdl_wait();
+  pdl_trigger();
   const long long row = blockIdx.x;  // over S * P
   const long long f = row / P;
   const int p = (int)(row % P);
@@ -80,10 +84,11 @@ int qvggt_patchify(const void* images, void* out, int64_t S, int32_t H, int32_t 
   const long long rows = S * (long long)(H / patch) * (W / patch);
   if (rows == 0) return QVGGT_OK;
   if (rows > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "patchify: too many patches");
-  patchify_kernel<<<(unsigned)rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(images), static_cast<__half*>(out), (int)S, H, W, patch, k_pad, mean3[0], mean3[1],
-      mean3[2], std3[0], std3[1], std3[2]);
-  int rc = check_cuda(cudaGetLastError(), "patchify launch");
+  int rc = check_cuda(launch_pdl(patchify_kernel, dim3((unsigned)rows), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                                 1u, static_cast<const __half*>(images), static_cast<__half*>(out), (int)S, (int)H,
+                                 (int)W, (int)patch, (int)k_pad, mean3[0], mean3[1], mean3[2], std3[0], std3[1],
+                                 std3[2]),
+                      "patchify launch");
   if (!rc) count_launch(1);
   return rc;
 }
@@ -98,10 +103,12 @@ int qvggt_assemble_tokens(const void* src, int64_t src_rows_per_frame, int64_t s
   if (n_special > 0 && !specials) return set_error(QVGGT_ERR_INVALID, "assemble_tokens: specials required");
   const long long rows = S * (long long)P;
   if (rows == 0) return QVGGT_OK;
-  assemble_kernel<<<(unsigned)rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(src), src_rows_per_frame, src_row_offset, static_cast<const __half*>(specials),
-      n_special, two_sets, static_cast<const __half*>(pos), static_cast<__half*>(out), P, C, frame_offset);
-  int rc = check_cuda(cudaGetLastError(), "assemble_tokens launch");
+  int rc = check_cuda(launch_pdl(assemble_kernel, dim3((unsigned)rows), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                                 1u, static_cast<const __half*>(src), (long long)src_rows_per_frame,
+                                 (long long)src_row_offset, static_cast<const __half*>(specials), (int)n_special,
+                                 (int)two_sets, static_cast<const __half*>(pos), static_cast<__half*>(out), (int)P,
+                                 (int)C, (long long)frame_offset),
+                      "assemble_tokens launch");
   if (!rc) count_launch(1);
   return rc;
 }
