@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(SA_WARPS * 32) attn_small_kernel(SmallAttnArgs
   uint32_t* vs = ks + SA_MAXL * SA_ROW;                // [L][SA_ROW]
   float* ps = reinterpret_cast<float*>(vs + SA_MAXL * SA_ROW);   // [SA_WARPS][L]
   uint32_t* qs = reinterpret_cast<uint32_t*>(ps + SA_WARPS * SA_MAXL);   // [SA_WARPS][64]
+  pdl_wait();
+  pdl_trigger();
 
   const int chunk = blockIdx.x % a.chunks;
   const int h = (blockIdx.x / a.chunks) % a.heads;
@@ -144,8 +146,9 @@ extern "C" int qvggt_attention_small(const void* q, int64_t q_stride, const void
   const int smem = (2 * SA_MAXL * SA_ROW + SA_WARPS * 64) * 4 + SA_WARPS * SA_MAXL * 4;
   static DeviceFlags attr_set;
   if (int rc = ensure_smem(attr_set, attn_small_kernel, smem, "cudaFuncSetAttribute(attention_small)")) return rc;
-  attn_small_kernel<<<(unsigned)grid, SA_WARPS * 32, smem, static_cast<cudaStream_t>(stream)>>>(a);
-  int rc = check_cuda(cudaGetLastError(), "attention_small launch");
+  int rc = check_cuda(launch_pdl(attn_small_kernel, dim3((unsigned)grid), dim3(SA_WARPS * 32), smem,
+                                 static_cast<cudaStream_t>(stream), 1u, a),
+                      "attention_small launch");
   if (!rc) count_launch(1);
   return rc;
 }

@@ -139,6 +139,10 @@ __global__ void __launch_bounds__(SCfg<MT, MODE>::THREADS)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // no global memory touched so far: wait for the previous kernel in the
+  // stream only now (programmatic dependent launch)
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -455,19 +459,9 @@ int launch_small(const GemmLaunch& L, const SmallPlan& P) {
   auto kfn = gemm_small_kernel<MT, MODE>;
   rc = ensure_smem_attr<MT, MODE>();
   if (rc) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(P.n_blocks * P.splits), 1, 1);
-  cfg.blockDim = dim3(C::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = L.stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)P.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, kfn, tmX, tmW, tmS, tmZ, sa), "gemm_small launch");
+  return check_cuda(launch_pdl(kfn, dim3((unsigned)(P.n_blocks * P.splits)), dim3(C::THREADS), C::SMEM, L.stream,
+                               (unsigned)P.splits, tmX, tmW, tmS, tmZ, sa),
+                    "gemm_small launch");
 }
 
 }  // namespace

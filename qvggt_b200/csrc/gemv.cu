@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, MT == 1 ? 2 : 1) gemv_w4_kern
   T* out = static_cast<T*>(out_);
   extern __shared__ __align__(16) uint8_t x_smem_raw[];   // XS: x [m, K]
   T* x_smem = reinterpret_cast<T*>(x_smem_raw);
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[GEMV_ROWS][4][4][MT];          // [row][quarter][channel][m]
   if constexpr (XS) {
     const int chunks = m * K / 8;
@@ -195,9 +197,10 @@ int gemv_launch(bool bf16, const void* in_feats, const void* qweight, const void
   // x staged in shared memory when it fits the default 48 KB with room to spare
   const int xs_bytes = (int)(m * K * 2);
   const bool xs = xs_bytes <= GEMV_XS_MAX;
+  cudaError_t err = cudaSuccess;
   auto args = [&](auto kfn) {
-    kfn<<<grid, block, xs ? xs_bytes : 0, st>>>(in_feats, static_cast<const uint16_t*>(qweight), scales,
-                                                 scaled_zeros, bias, out, (int)m, (int)N, (int)K, group_size);
+    err = launch_pdl(kfn, grid, block, xs ? xs_bytes : 0, st, 1u, in_feats, static_cast<const uint16_t*>(qweight),
+                     scales, scaled_zeros, bias, out, (int)m, (int)N, (int)K, (int)group_size);
   };
   auto by_m = [&](auto mt) {
     constexpr int MT = decltype(mt)::value;
@@ -215,7 +218,7 @@ int gemv_launch(bool bf16, const void* in_feats, const void* qweight, const void
   else if (m <= 4) by_m(std::integral_constant<int, 4>());
   else if (m <= 8) by_m(std::integral_constant<int, 8>());
   else by_m(std::integral_constant<int, 16>());
-  int rc = check_cuda(cudaGetLastError(), "gemv launch");
+  int rc = check_cuda(err, "gemv launch");
   if (rc == QVGGT_OK) count_launch(1);
   return rc;
 }

@@ -83,6 +83,8 @@ template <int CH, bool PER_TOKEN>
 __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32) layernorm_quant_kernel(
     const __half* __restrict__ x, const __half* __restrict__ w, const __half* __restrict__ b,
     int8_t* __restrict__ out, __half* __restrict__ scale, long long T, float eps) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int H = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROWS_PER_BLOCK + (threadIdx.x >> 5);
@@ -144,6 +146,8 @@ template <int CH>
 __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32) quant_kernel(const __half* __restrict__ x,
                                                                     int8_t* __restrict__ out,
                                                                     __half* __restrict__ scale, long long T) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int H = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROWS_PER_BLOCK + (threadIdx.x >> 5);
@@ -190,6 +194,8 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 32) gelu_quant_kernel(const _
                                                                          int8_t* __restrict__ out,
                                                                          __half* __restrict__ scale,
                                                                          __half* __restrict__ tmp, long long T) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int H = CH * 256;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROWS_PER_BLOCK + (threadIdx.x >> 5);
@@ -305,16 +311,20 @@ int qvggt_layernorm_quant(int8_t* out, const void* in, const void* gamma, const 
     return set_error(QVGGT_ERR_INVALID, "layernorm_quant: gamma, scale (and beta per-token) required");
   if (tokens == 0) return QVGGT_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaSuccess;
+  const dim3 grid(rows_grid(tokens)), block(ROWS_PER_BLOCK * 32);
   if (per_token) {
-    QV_DISPATCH_CH_SMALL(hidden, (layernorm_quant_kernel<CH, true><<<rows_grid(tokens), ROWS_PER_BLOCK * 32, 0, st>>>(
-                               static_cast<const __half*>(in), static_cast<const __half*>(gamma),
-                               static_cast<const __half*>(beta), out, static_cast<__half*>(scale_io), tokens, eps)));
+    QV_DISPATCH_CH_SMALL(hidden, err = launch_pdl(layernorm_quant_kernel<CH, true>, grid, block, 0, st, 1u,
+                                                  static_cast<const __half*>(in), static_cast<const __half*>(gamma),
+                                                  static_cast<const __half*>(beta), out,
+                                                  static_cast<__half*>(scale_io), (long long)tokens, eps));
   } else {
-    QV_DISPATCH_CH_SMALL(hidden, (layernorm_quant_kernel<CH, false><<<rows_grid(tokens), ROWS_PER_BLOCK * 32, 0, st>>>(
-                               static_cast<const __half*>(in), static_cast<const __half*>(gamma), nullptr, out,
-                               static_cast<__half*>(scale_io), tokens, eps)));
+    QV_DISPATCH_CH_SMALL(hidden, err = launch_pdl(layernorm_quant_kernel<CH, false>, grid, block, 0, st, 1u,
+                                                  static_cast<const __half*>(in), static_cast<const __half*>(gamma),
+                                                  static_cast<const __half*>(nullptr), out,
+                                                  static_cast<__half*>(scale_io), (long long)tokens, eps));
   }
-  rc = check_cuda(cudaGetLastError(), "layernorm_quant launch");
+  rc = check_cuda(err, "layernorm_quant launch");
   if (!rc) count_launch(1);
   return rc;
 }
@@ -324,9 +334,11 @@ int qvggt_invoke_quant(int8_t* out, const void* in, void* scale, int64_t tokens,
   if (rc) return rc;
   if (tokens == 0) return QVGGT_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  QV_DISPATCH_CH(hidden, quant_kernel<CH><<<rows_grid(tokens), ROWS_PER_BLOCK * 32, 0, st>>>(
-                             static_cast<const __half*>(in), out, static_cast<__half*>(scale), tokens));
-  rc = check_cuda(cudaGetLastError(), "invoke_quant launch");
+  cudaError_t err = cudaSuccess;
+  QV_DISPATCH_CH(hidden, err = launch_pdl(quant_kernel<CH>, dim3(rows_grid(tokens)), dim3(ROWS_PER_BLOCK * 32), 0, st,
+                                          1u, static_cast<const __half*>(in), out, static_cast<__half*>(scale),
+                                          (long long)tokens));
+  rc = check_cuda(err, "invoke_quant launch");
   if (!rc) count_launch(1);
   return rc;
 }
@@ -337,10 +349,11 @@ int qvggt_gelu_quant(int8_t* out, const void* in, void* scale, void* tmp, int64_
   if (!aligned16(tmp)) return set_error(QVGGT_ERR_ALIGN, "gelu_quant: tmp must be 16-byte aligned");
   if (tokens == 0) return QVGGT_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  QV_DISPATCH_CH(d, gelu_quant_kernel<CH><<<rows_grid(tokens), ROWS_PER_BLOCK * 32, 0, st>>>(
-                        static_cast<const __half*>(in), out, static_cast<__half*>(scale), static_cast<__half*>(tmp),
-                        tokens));
-  rc = check_cuda(cudaGetLastError(), "gelu_quant launch");
+  cudaError_t err = cudaSuccess;
+  QV_DISPATCH_CH(d, err = launch_pdl(gelu_quant_kernel<CH>, dim3(rows_grid(tokens)), dim3(ROWS_PER_BLOCK * 32), 0, st,
+                                     1u, static_cast<const __half*>(in), out, static_cast<__half*>(scale),
+                                     static_cast<__half*>(tmp), (long long)tokens));
+  rc = check_cuda(err, "gelu_quant launch");
   if (!rc) count_launch(1);
   return rc;
 }

@@ -19,6 +19,8 @@ namespace {
 
 __global__ void pose_kernel(const float* __restrict__ pe, long long n, float h, float w, float* __restrict__ ext,
                             float* __restrict__ intr) {
+  pdl_wait();
+  pdl_trigger();
   const long long f = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= n) return;
   const float* p = pe + f * 9;
@@ -81,6 +83,8 @@ __device__ __forceinline__ float3 unproject_one(long long idx, float d, int H, i
 __global__ void unproject_kernel(const float* __restrict__ depth, long long total, int H, int W,
                                  const float* __restrict__ ext, const float* __restrict__ intr,
                                  float* __restrict__ pts) {
+  pdl_wait();
+  pdl_trigger();
   const long long groups = total / 4;
   for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < groups;
        g += (long long)gridDim.x * blockDim.x) {
@@ -121,9 +125,9 @@ int qvggt_pose_encoding_to_extri_intri(const float* pose_enc, int64_t n, int32_t
   if (!pose_enc || !extrinsics) return set_error(QVGGT_ERR_INVALID, "pose_encoding_to_extri_intri: null tensor");
   const long long blocks = (n + 127) / 128;
   if (blocks > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "pose_encoding_to_extri_intri: n too large");
-  pose_kernel<<<(unsigned)blocks, 128, 0, static_cast<cudaStream_t>(stream)>>>(pose_enc, n, (float)image_h,
-                                                                                (float)image_w, extrinsics, intrinsics);
-  int rc = check_cuda(cudaGetLastError(), "pose_encoding_to_extri_intri launch");
+  int rc = check_cuda(launch_pdl(pose_kernel, dim3((unsigned)blocks), dim3(128), 0, static_cast<cudaStream_t>(stream), 1u,
+                                 pose_enc, (long long)n, (float)image_h, (float)image_w, extrinsics, intrinsics),
+                      "pose_encoding_to_extri_intri launch");
   if (!rc) count_launch(1);
   return rc;
 }
@@ -142,9 +146,10 @@ int qvggt_unproject_depth(const float* depth, int64_t S, int32_t H, int32_t W, c
   const long long cap = 8LL * di.num_sms;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  unproject_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(depth, total, H, W, extrinsics,
-                                                                                   intrinsics, world_points);
-  int rc = check_cuda(cudaGetLastError(), "unproject_depth launch");
+  int rc = check_cuda(launch_pdl(unproject_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                                 static_cast<cudaStream_t>(stream), 1u, depth, total, (int)H, (int)W, extrinsics,
+                                 intrinsics, world_points),
+                      "unproject_depth launch");
   if (!rc) count_launch(1);
   return rc;
 }

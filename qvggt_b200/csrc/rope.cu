@@ -19,6 +19,8 @@ __global__ void rope_with_pos_kernel(const __half* __restrict__ in, const float*
                                      __half* __restrict__ out, int S, int h, int d, int d2, long long is_s,
                                      long long is_b, long long is_h, long long is_d, long long os_s, long long os_b,
                                      long long os_h, long long os_d) {
+  pdl_wait();
+  pdl_trigger();
   const int s_id = blockIdx.x, b_id = blockIdx.y;
   const __half* src = in + s_id * is_s + b_id * is_b;
   __half* dst = out + s_id * os_s + b_id * os_b;
@@ -78,6 +80,8 @@ __device__ __forceinline__ void rope_half(const float* x, float* y, const __half
 }
 
 __global__ void __launch_bounds__(128) qkv_rope2d_kernel(Rope2dArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_tok = 3 * a.heads;
   const long long t = gid / per_tok;
@@ -146,10 +150,13 @@ int qvggt_rope_with_pos(const void* in, const float* freqs, void* out, int64_t s
   if (s == 0 || b == 0) return QVGGT_OK;
   if (s > 2147483647 || b > 65535) return set_error(QVGGT_ERR_UNSUPPORTED, "rope_with_pos: grid too large");
   const int warps = h < 16 ? 4 : 8;  // launch shape as fused_rope_with_pos.cu:80-82
-  rope_with_pos_kernel<<<dim3((unsigned)s, (unsigned)b), dim3(32, warps), 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(in), freqs, static_cast<__half*>(out), (int)s, (int)h, (int)d, (int)d2, in_strides[0],
-      in_strides[1], in_strides[2], in_strides[3], out_strides[0], out_strides[1], out_strides[2], out_strides[3]);
-  int rc = check_cuda(cudaGetLastError(), "rope_with_pos launch");
+  int rc = check_cuda(
+      launch_pdl(rope_with_pos_kernel, dim3((unsigned)s, (unsigned)b), dim3(32, warps), 0,
+                 static_cast<cudaStream_t>(stream), 1u, static_cast<const __half*>(in), freqs, static_cast<__half*>(out),
+                 (int)s, (int)h, (int)d, (int)d2, (long long)in_strides[0], (long long)in_strides[1],
+                 (long long)in_strides[2], (long long)in_strides[3], (long long)out_strides[0],
+                 (long long)out_strides[1], (long long)out_strides[2], (long long)out_strides[3]),
+      "rope_with_pos launch");
   if (!rc) count_launch(1);
   return rc;
 }
@@ -186,8 +193,8 @@ int qvggt_qkv_rope2d(const void* qkv, void* q_out, void* kv_out, int64_t T, int3
   a.eps = eps;
   const long long threads = T * 3 * heads;
   const unsigned blocks = (unsigned)((threads + 127) / 128);
-  qkv_rope2d_kernel<<<blocks, 128, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  int rc = check_cuda(cudaGetLastError(), "qkv_rope2d launch");
+  int rc = check_cuda(launch_pdl(qkv_rope2d_kernel, dim3(blocks), dim3(128), 0, static_cast<cudaStream_t>(stream), 1u, a),
+                      "qkv_rope2d launch");
   if (!rc) count_launch(1);
   return rc;
 }
