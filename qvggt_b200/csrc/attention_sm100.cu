@@ -63,11 +63,12 @@ struct AttnSmem {
   static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
   // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], s_free[2], p_full[2],
   // o_done[2], drain (S issuer), drain2 (PV issuer)
-  static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 2;
+  static constexpr int NUM_BARS = 1 + 4 * KV_STAGES + 8 + 2 + 1;
   static constexpr int MISC = BAR + NUM_BARS * 8;
   // MISC: +0 TMEM base, +4 abort flag, +8 status word pointer, +16 timeout (ns),
-  // +24 "this CTA merges the splits" flag, +28 first key tile of this CTA
-  static constexpr int TOTAL = MISC + 32 + 1024;
+  // +24 "this CTA merges the splits" flag, +28 first key tile of this CTA,
+  // +32 + 4w the item softmax warp w (0..7) is on
+  static constexpr int TOTAL = MISC + 64 + 1024;
 };
 
 struct AttnArgs {
@@ -321,24 +322,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* o_done = p_full + 2;            // [2] MMA -> softmax: PV_i complete
   uint64_t* drain = o_done + 2;
   uint64_t* drain2 = drain + 1;
+  uint64_t* q_empty = drain2 + 1;           // S issuer -> Q producer: the item's S MMAs done with Q
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AttnSmem::MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + AttnSmem::MISC + 4);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int sp = blockIdx.x % a.splits;          // KV split of this CTA
-  const int item = blockIdx.x / a.splits;        // (batch, head, query block)
-  const int qb = item % a.nqb;
-  const int h = (item / a.nqb) % a.heads;
-  const int b = item / (a.nqb * a.heads);
-  const long long q_row0 = (long long)b * a.Lq + (long long)qb * 256;   // first query row of this CTA
-  const long long kv_row0 = (long long)b * a.Lkv;
+  // Work items are (batch, head, query block).  The plain kernel is
+  // persistent: CTA x takes items x, x + gridDim.x, ... one after another,
+  // every role walking the same sequence, so the next item's Q and first
+  // K / V tiles load and its first S MMAs run while the current item's last
+  // tiles and epilogue finish.  The general kernel takes one item per CTA.
+  const int n_items = a.batches * a.heads * a.nqb;
+  const int item0 = blockIdx.x / a.splits;
+  const int item_step = GENERAL ? n_items : (int)gridDim.x;
   int t_first, t_end;
   split_range(a, sp, t_first, t_end);
-  const int nkv = t_end - t_first;               // KV tiles of this CTA
-  // Q tiles of this CTA that hold rows of its batch (the last block of a
-  // batch may end inside tile 0, e.g. 1374 = 5 x 256 + 94): an empty tile 1
-  // gets no MMAs and no softmax.
-  const int nqt = ((long long)qb * 256 + 128 < a.Lq) ? 2 : 1;
+  const int nkv = t_end - t_first;               // KV tiles of this CTA, per item
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(drain, 1);
     mbar_init(drain2, 1);
+    mbar_init(q_empty, 1);
     *abort_flag = 0;
     *reinterpret_cast<uint32_t**>(smem + AttnSmem::MISC + 8) = a.ctl.status;
     *reinterpret_cast<unsigned long long*>(smem + AttnSmem::MISC + 16) = a.ctl.timeout_ns;
@@ -398,24 +399,34 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       uint8_t* base = smem + (is_k ? AttnSmem::K : AttnSmem::V);
-      if (is_k) {
-        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-        tma_load_3d(smem + AttnSmem::Q0, &tmQ, q_full, 0, h, (int)q_row0);
-        tma_load_3d(smem + AttnSmem::Q1, &tmQ, q_full, 0, h, (int)(q_row0 + 128));
+      int jg = 0, it = 0;   // ring slots used, items started
+      bool ok = true;
+      for (int item = item0; ok && item < n_items; item += item_step, ++it) {
+        const int qb = item % a.nqb;
+        const int h = (item / a.nqb) % a.heads;
+        const long long b = item / (a.nqb * a.heads);
+        if (is_k) {
+          // Q of the previous item is free once its S MMAs are done
+          if (it > 0 && !wait(q_empty, (it - 1) & 1, misc, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+          const long long q_row0 = b * a.Lq + (long long)qb * 256;
+          mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+          tma_load_3d(smem + AttnSmem::Q0, &tmQ, q_full, 0, h, (int)q_row0);
+          tma_load_3d(smem + AttnSmem::Q1, &tmQ, q_full, 0, h, (int)(q_row0 + 128));
+        }
+        const long long kv_row0 = b * a.Lkv;
+        for (int j = 0; j < nkv; ++j, ++jg) {
+          const int st = jg % KV_STAGES;
+          const uint32_t ph = (jg / KV_STAGES) & 1;
+          if (!wait(&empty[st], ph ^ 1, misc, ST_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+          const int row = (int)(kv_row0 + tile_row(a, t_first + j));
+          mbar_arrive_expect_tx(&full[st], TILE_BYTES);
+          tma_load_3d(base + st * TILE_BYTES, tm, &full[st], 0, h, row);
+        }
       }
-      int j = 0;
-      for (; j < nkv; ++j) {
-        const int st = j % KV_STAGES;
-        const uint32_t ph = (j / KV_STAGES) & 1;
-        if (!wait(&empty[st], ph ^ 1, misc, ST_TIMEOUT_TMA_EMPTY)) break;
-        const int row = (int)(kv_row0 + tile_row(a, t_first + j));
-        mbar_arrive_expect_tx(&full[st], TILE_BYTES);
-        tma_load_3d(base + st * TILE_BYTES, tm, &full[st], 0, h, row);
-      }
-      if (j < nkv) {
+      if (!ok) {
         // aborted: let the loads already issued land before the CTA exits
-        if (is_k) mbar_wait_drain(q_full, 0, 200000000ull);
-        for (int jj = (j > KV_STAGES ? j - KV_STAGES : 0); jj < j; ++jj)
+        if (is_k && it > 0) mbar_wait_drain(q_full, (it - 1) & 1, 200000000ull);
+        for (int jj = (jg > KV_STAGES ? jg - KV_STAGES : 0); jj < jg; ++jj)
           mbar_wait_drain(&full[jj % KV_STAGES], (jj / KV_STAGES) & 1, 200000000ull);
       }
     }
@@ -428,24 +439,37 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, 128);
       const uint32_t q_addr[2] = {smem_u32(smem + AttnSmem::Q0), smem_u32(smem + AttnSmem::Q1)};
-      bool ok = wait(q_full, 0, misc, ST_TIMEOUT_FULL);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % KV_STAGES;
-        if (!wait(&k_full[st], (j / KV_STAGES) & 1, misc, ST_TIMEOUT_FULL)) { ok = false; break; }
-        const uint32_t k_addr = smem_u32(smem + AttnSmem::K + st * TILE_BYTES);
-        for (int i = 0; i < nqt; ++i) {
-          if (j > 0 && !wait(&s_free[i], (j - 1) & 1, misc, ST_TIMEOUT_SOFTMAX)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+      uint32_t cs[2] = {0, 0};   // S_i tiles issued so far (across items)
+      int jg = 0, it = 0;
+      bool ok = true;
+      for (int item = item0; ok && item < n_items; item += item_step, ++it) {
+        // Q tiles of the item that hold rows of its batch (the last block of
+        // a batch may end inside tile 0, e.g. 1374 = 5 x 256 + 94): an empty
+        // tile 1 gets no MMAs and no softmax
+        const int nqt = ((long long)(item % a.nqb) * 256 + 128 < a.Lq) ? 2 : 1;
+        if (!wait(q_full, it & 1, misc, ST_TIMEOUT_FULL)) { ok = false; break; }
+        for (int j = 0; j < nkv; ++j, ++jg) {
+          const int st = jg % KV_STAGES;
+          if (!wait(&k_full[st], (jg / KV_STAGES) & 1, misc, ST_TIMEOUT_FULL)) { ok = false; break; }
+          const uint32_t k_addr = smem_u32(smem + AttnSmem::K + st * TILE_BYTES);
+          for (int i = 0; i < nqt; ++i) {
+            // S_i is free once softmax i has read the previous S_i
+            if (cs[i] > 0 && !wait(&s_free[i], (cs[i] - 1) & 1, misc, ST_TIMEOUT_SOFTMAX)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f16_ss(tmem + COL_S0 + i * 128, sdesc_sw128(q_addr[i] + k * 32), sdesc_sw128(k_addr + k * 32),
-                       idesc_s, k > 0 ? 1u : 0u);
-          tc_commit(&s_full[i]);
+            for (int k = 0; k < 4; ++k)
+              mma_f16_ss(tmem + COL_S0 + i * 128, sdesc_sw128(q_addr[i] + k * 32), sdesc_sw128(k_addr + k * 32),
+                         idesc_s, k > 0 ? 1u : 0u);
+            tc_commit(&s_full[i]);
+            ++cs[i];
+          }
+          if (!ok) break;
+          tc_commit(&k_empty[st]);
         }
-        if (ok) tc_commit(&k_empty[st]);
+        if (ok) tc_commit(q_empty);   // the item's S MMAs are the last readers of its Q
       }
       if (!ok) {
         tc_commit(drain);
@@ -456,24 +480,31 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ O += P V issuer
     if (lane == 0) {
       constexpr uint32_t idesc_o = idesc_f16(128, 64, false, true);   // B = V, MN-major
+      uint32_t cp[2] = {0, 0};   // PV_i tiles issued so far (across items)
+      int jg = 0;
       bool ok = true;
-      for (int jj = 0; ok && jj < nkv; ++jj) {
-        const int st = jj % KV_STAGES;
-        const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
-        for (int i = 0; i < nqt; ++i) {
-          if (!wait(&p_full[i], jj & 1, misc, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
-          if (i == 0 && !wait(&v_full[st], (jj / KV_STAGES) & 1, misc, ST_TIMEOUT_FULL)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+      for (int item = item0; ok && item < n_items; item += item_step) {
+        const int nqt = ((long long)(item % a.nqb) * 256 + 128 < a.Lq) ? 2 : 1;
+        for (int jj = 0; jj < nkv; ++jj, ++jg) {
+          const int st = jg % KV_STAGES;
+          const uint32_t v_addr = smem_u32(smem + AttnSmem::V + st * TILE_BYTES);
+          for (int i = 0; i < nqt; ++i) {
+            if (!wait(&p_full[i], cp[i] & 1, misc, ST_TIMEOUT_SOFTMAX)) { ok = false; break; }
+            if (i == 0 && !wait(&v_full[st], (jg / KV_STAGES) & 1, misc, ST_TIMEOUT_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            mma_f16_ts(tmem + COL_O0 + i * 64, tmem + COL_P0 + i * 64 + k * 8, sdesc_sw128(v_addr + k * 2048),
-                       idesc_o, (jj > 0 || k > 0) ? 1u : 0u);
-          tc_commit(&o_done[i]);
+            for (int k = 0; k < 8; ++k)
+              mma_f16_ts(tmem + COL_O0 + i * 64, tmem + COL_P0 + i * 64 + k * 8, sdesc_sw128(v_addr + k * 2048),
+                         idesc_o, (jj > 0 || k > 0) ? 1u : 0u);
+            tc_commit(&o_done[i]);
+            ++cp[i];
+          }
+          if (!ok) break;
+          tc_commit(&v_empty[st]);
         }
-        if (ok) tc_commit(&v_empty[st]);
       }
       if (!ok) {
         tc_commit(drain2);
@@ -494,10 +525,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float c = a.scale_log2;
     const uint32_t bar_s_full = smem_u32(&s_full[i]);
     const uint32_t bar_s_free = bar_s_full + 16, bar_p_full = bar_s_full + 32, bar_o_done = bar_s_full + 48;
+    uint32_t cnt = 0;   // S_i tiles taken so far (across items)
+    bool ok = true;
+    // the warp's current item lives in shared memory, not in a register held
+    // through the tile loop (that pushed parts of the score row to local memory)
+#define QV_ITEM_SLOT (misc + 32 + ((threadIdx.x >> 5) - 4) * 4)
+    if (lane == 0) asm volatile("st.shared.s32 [%0], %1;" ::"r"(QV_ITEM_SLOT), "r"(item0) : "memory");
+    __syncwarp();
+    for (;;) {
+    int item;
+    asm volatile("ld.shared.s32 %0, [%1];" : "=r"(item) : "r"(QV_ITEM_SLOT) : "memory");
+    if (!ok || item >= a.batches * a.heads * a.nqb) break;
+    // a Q tile past the end of its batch has no MMAs; its warpgroup still
+    // runs the epilogue (with nothing to store) so the split merge's named
+    // barriers see both warpgroups
+    const int nkv_i = i < (((long long)(item % a.nqb) * 256 + 128 < a.Lq) ? 2 : 1) ? nkv : 0;
     float m_used = -INFINITY, l = 0.f;
-    bool ok = i < nqt;
-    for (int j = 0; ok && j < nkv; ++j) {
-      if (!softmax_wait(bar_s_full, j & 1, misc)) { ok = false; break; }
+    for (int j = 0; ok && j < nkv_i; ++j, ++cnt) {
+      if (!softmax_wait(bar_s_full, cnt & 1, misc)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[128];
       load_s_row(tS, s);
@@ -525,8 +570,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         rescale = j > 0;
         m_used = m_target;
       }
-      const uint32_t o_par = (uint32_t)(j - 1) & 1;
-      const bool o_ready = j == 0;   // PV_i(j-1) complete (nothing to wait for at j = 0)
+      const uint32_t o_par = (cnt - 1) & 1;
+      // PV_i(j-1) complete (nothing to wait for at j = 0: the previous item's
+      // epilogue has waited for its last PV)
+      const bool o_ready = j == 0;
       const float lj = (valid == 128)
           ? exp_store<false, POLY>(s, c, -m_used, valid, tP, o_ready, bar_o_done, o_par, misc)
           : exp_store<true, POLY>(s, c, -m_used, valid, tP, o_ready, bar_o_done, o_par, misc);
@@ -552,16 +599,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     // `have`: O_i of the last tile is complete (warp-uniform, so the
     // warp-collective TMEM loads below run in whole warps).
     bool have = false;
-    if (ok && nkv > 0) {
-      have = softmax_wait(bar_o_done, (nkv - 1) & 1, misc);
+    if (ok && nkv_i > 0) {
+      have = softmax_wait(bar_o_done, (cnt - 1) & 1, misc);
       if (have) tc_fence_after();
     }
-    // the CTA's coordinates are re-derived here (a volatile read of
-    // %ctaid.x) rather than kept in registers through the loop
+    // the split and the item are re-read here (%ctaid.x, shared memory)
+    // rather than kept in registers through the loop
     uint32_t cta;
     asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(cta));
     const uint32_t sp_e = cta % (uint32_t)a.splits;
-    const uint32_t item_e = cta / (uint32_t)a.splits;
+    uint32_t item_e;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(item_e) : "r"(QV_ITEM_SLOT) : "memory");
     const int qb_e = (int)(item_e % (uint32_t)a.nqb);
     const int h_e = (int)((item_e / (uint32_t)a.nqb) % (uint32_t)a.heads);
     const long long b_e = item_e / ((uint32_t)a.nqb * (uint32_t)a.heads);
@@ -714,6 +762,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (row_ok && a.lse_mode != 0) a.lse[bhq] = (lmax + log2f(wsum)) * 0.6931471805599453f;
       }
     }
+    __syncwarp();
+    if (lane == 0)
+      asm volatile("st.shared.s32 [%0], %1;" ::"r"(QV_ITEM_SLOT),
+                   "r"((int)item_e + (GENERAL ? a.batches * a.heads * a.nqb : (int)gridDim.x))
+                   : "memory");
+    __syncwarp();
+#undef QV_ITEM_SLOT
+    }   // items
   }
 
   tc_fence_before();
@@ -858,8 +914,8 @@ int attention_launch(const void* q, int64_t q_stride, const void* kv, int64_t kv
   a.part_o = splits > 1 ? reinterpret_cast<float*>(sc + SL.part_o) : nullptr;
   a.scale_log2 = 0.125f * 1.4426950408889634f;
   a.ctl = make_ctl();
-  const long long grid = (long long)a.nqb * heads * batches * splits;
-  if (grid > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
+  const long long items = (long long)a.nqb * heads * batches;
+  if (items * splits > 2147483647LL) return set_error(QVGGT_ERR_UNSUPPORTED, "attention: grid too large");
   // Share of exponentials computed on the FMA pipe (pairs per 8).  Measured
   // on B200 with the split S / PV issuers: 1 is fastest at the aggregator's
   // L = 43,968 (811 TFLOP/s vs 780 for 0 and 800 for 2); the QVGGT_ATTN_POLY
@@ -869,6 +925,10 @@ int attention_launch(const void* q, int64_t q_stride, const void* kv, int64_t kv
     return (e && e[0] >= '0' && e[0] <= '4') ? e[0] - '0' : 1;
   }();
   const bool general = splits > 1 || lse_mode != 0;
+  // general: one CTA per (item, split); plain: persistent, one CTA per SM
+  // (the kernel's shared memory allows one) walking items gridDim.x apart
+  const long long sms = device_info().num_sms;
+  const long long grid = general ? items * splits : (items < sms ? items : sms);
   using Kfn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AttnArgs);
   static const Kfn plain_fns[5] = {attn_fwd_kernel<0, false>, attn_fwd_kernel<1, false>, attn_fwd_kernel<2, false>,
                                    attn_fwd_kernel<3, false>, attn_fwd_kernel<4, false>};
