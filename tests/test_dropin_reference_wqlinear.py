@@ -2,7 +2,8 @@
 
 The reference's ``qvggt/runtime/awq/qmodule.py`` is imported from the reference
 checkout with ``sys.modules["awq_inference_engine"]`` set to
-``qvggt_b200.awq_inference_engine`` (the switch INTEGRATION.md describes).
+``qvggt_b200.awq_inference_engine`` (the one-line switch a QVGGT maintainer
+makes to use this library).
 Without a GPU, the shim's CUDA-only guards are relaxed and the C-ABI call is
 recorded instead of made; the test then checks that ``WQLinear.forward``
 (``qmodule.py:333-369``) reaches ``gemv_forward_cuda_new`` for fewer than 8
